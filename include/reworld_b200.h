@@ -1,0 +1,162 @@
+/*
+ * reworld_b200 — C ABI of the B200 (sm_100a) kernels for ReWorld's per-chunk
+ * causal self-attention hot path (Wan2.2-TI2V-5B DiT, KV cache + landmark bank).
+ *
+ * All entry points take plain device pointers, sizes and element strides, run
+ * on the CUDA stream passed as `stream` (a cudaStream_t; NULL = legacy default
+ * stream), never allocate device memory and return RW_OK (0) or a negative
+ * RW_ERR_* code.  Asynchronous failures inside a kernel (a bounded wait that
+ * ran out of time) are reported through the optional device `status` word as
+ * RW_STATUS_* bits; kernels never trap.
+ *
+ * bf16 tensors use the reference's [B, L, H, D] layout with a contiguous head
+ * dimension; the other three strides are given in elements.
+ */
+#ifndef REWORLD_B200_H
+#define REWORLD_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes --------------------------------------------------------- */
+#define RW_OK 0
+#define RW_ERR_INVALID_ARG (-1)  /* null pointer, bad size, misaligned pointer/stride */
+#define RW_ERR_UNSUPPORTED (-2)  /* e.g. head_dim != 128 */
+#define RW_ERR_CUDA (-3)         /* a CUDA runtime call failed (launch error) */
+#define RW_ERR_DRIVER (-4)       /* TMA descriptor encoding failed */
+#define RW_ERR_CAPACITY (-5)     /* request exceeds a fixed capacity */
+
+/* ---- device status word bits (atomicOr'ed into *status) -------------------- */
+#define RW_STATUS_TIMEOUT_LOAD 0x01     /* TMA producer wait ran out of time */
+#define RW_STATUS_TIMEOUT_MMA 0x02      /* MMA issuer wait ran out of time */
+#define RW_STATUS_TIMEOUT_SOFTMAX 0x04  /* softmax/epilogue wait ran out of time */
+#define RW_STATUS_TIMEOUT_COPY 0x08     /* bulk-copy wait ran out of time */
+#define RW_STATUS_BAD_SLOT 0x10         /* a descriptor/slot index was out of range */
+
+/* 3-D RoPE parameters (the reference's causal_rope_apply + pm_rope_delta_apply).
+ * freqs: the model's complex128 table [max_pos][64] stored as (real, imag)
+ * double pairs (wan_5b/modules/causal_model.py:790-807, model.py:29-39).
+ * Token t of the chunk (t < grid_f*grid_h*grid_w) rotates complex pair j by
+ * freqs[start_frame + t/(h*w)][j] for j < c_t, freqs[(t/w)%h][j] for
+ * c_t <= j < c_t+c_h and freqs[t%w][j] otherwise; tokens past f*h*w are left
+ * unchanged (causal_model.py:156-184).  The rotation is done in fp64 and rounded
+ * to bf16 through fp32 as the reference's .type_as() does.  delta_cs, when not
+ * NULL, holds the PM-RoPE phase as fp32 (cos, sin) pairs [B][grid_f][64] and is
+ * applied after that rounding, in fp32, then rounded to bf16 again
+ * (wan_5b/modules/action_model.py:40-51). */
+typedef struct rw_rope {
+  const double* freqs;
+  int max_pos;
+  int start_frame;
+  int grid_f, grid_h, grid_w;
+  int c_t, c_h, c_w;
+  const float* delta_cs;
+} rw_rope_t;
+
+/* Chunk attention forward: o = softmax(q k^T * softmax_scale) v per (batch, head),
+ * non-causal, bf16 in/out, fp32 accumulation (tcgen05/TMEM, TMA-fed).
+ * Replaces wan_5b/modules/attention.py:133-179 `attention(q, k, v)` (and the
+ * flash_attn_varlen_func call at :111-127) as called from
+ * wan_5b/modules/action_model.py:302 with k/v = kv_cache[:, :local_end].
+ * q,o: [B, Lq, H, 128]; k,v: [B, Lk, H, 128].  If rope != NULL the 3-D RoPE
+ * (+ PM-RoPE phase) is applied to q inside the kernel before QK^T (the
+ * reference applies it at action_model.py:265-275 before the call).
+ * Requirements: head_dim 128, all pointers 16-byte aligned, strides multiples
+ * of 8 elements, Lq >= 1, Lk >= 1, softmax_scale > 0. */
+int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, int D,
+                long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh,
+                long long v_sb, long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh,
+                float softmax_scale, const rw_rope_t* rope, int* status, void* stream);
+
+/* RoPE(+PM-RoPE) on the new chunk's K and the cache write of K and V:
+ * cache_k[b, dst_start + t] = rope(k[b, t]), cache_v[b, dst_start + t] = v[b, t]
+ * for t < L; optionally q_out[b, t] = rope(q_in[b, t]) when q_in != NULL.
+ * Replaces wan_5b/modules/action_model.py:265-292 (causal_rope_apply on q/k,
+ * pm_rope_delta_apply, and the kv_cache["k"/"v"][:, a:b] = ... writes).
+ * rope may be NULL (plain copy).  Element strides as in rw_attn_fwd. */
+int rw_rope_kv_store(const void* k, const void* v, const void* q_in, void* q_out, void* cache_k, void* cache_v,
+                     int B, int L, int H, int D, int dst_start, long long k_sb, long long k_sl, long long k_sh,
+                     long long v_sb, long long v_sl, long long v_sh, long long q_sb, long long q_sl,
+                     long long q_sh, long long qo_sb, long long qo_sl, long long qo_sh, long long ck_sb,
+                     long long ck_sl, long long ck_sh, long long cv_sb, long long cv_sl, long long cv_sh,
+                     const rw_rope_t* rope, void* stream);
+
+/* One byte-copy job of the landmark/cache assembly: nbytes from src to dst,
+ * both 16-byte aligned, nbytes a multiple of 16. */
+typedef struct rw_copy_desc {
+  const void* src;
+  void* dst;
+  long long nbytes;
+} rw_copy_desc_t;
+
+/* Executes n copy jobs (descriptor array in DEVICE memory) with one launch of a
+ * TMA bulk-copy (cp.async.bulk) kernel: the landmark gather of
+ * longctx/inference/landmark_cache_v2.py:618-682 (write_into_cache, direct-write
+ * path) and :362-397 (read_pair_into), for all layers at once.  Jobs must not
+ * overlap each other's destinations.  Bit-exact byte copies. */
+int rw_copy_chunks(const rw_copy_desc_t* descs, int n, int* status, void* stream);
+
+/* Landmark-bank decision state in device memory (all fields written only by
+ * rw_bank_step; zero-initialise before the first call).  Capacity RW_BANK_MAX. */
+#define RW_BANK_MAX 1024
+typedef struct rw_bank_state {
+  int n;          /* members in the bank (list order = admission order minus evictions) */
+  int admitted;   /* members ever admitted (drives protect-earliest-n) */
+  int pad[2];
+  double tx[RW_BANK_MAX], ty[RW_BANK_MAX], tz[RW_BANK_MAX]; /* translation of each member's pose */
+  double yaw[RW_BANK_MAX];                                  /* degrees(atan2(R02, R22)) */
+  int born[RW_BANK_MAX];
+  int slot[RW_BANK_MAX];                                    /* caller's storage slot of the member */
+  int prot[RW_BANK_MAX];                                    /* 1 = protected from eviction */
+} rw_bank_state_t;
+
+/* Result of one rw_bank_step (device memory). */
+typedef struct rw_bank_result {
+  int n_evicted;
+  int evicted_born[4];
+  int evicted_slot[4];
+  int n_bank;          /* bank size after the step */
+  int nR;              /* number of retrieved members */
+  int R[RW_BANK_MAX];  /* retrieved bank-list indices, ascending */
+  int R_slot[RW_BANK_MAX];
+} rw_bank_result_t;
+
+/* One bank decision, single warp-level kernel, fp64:
+ *  (1) when admit != 0: while the bank holds >= K members evict the member
+ *      chosen by landmark_cache_v2.py:465-479 (_evict_index: protect the first
+ *      protect_n admitted, else smallest nearest-neighbour pose distance, ties
+ *      evict the later-born), then append {admit_pose12, admit_born,
+ *      admit_slot} (:481-495 _bank_insert, always-admit);
+ *  (2) retrieval (:538-592 _retrieve, plain top-k by pose_dist of
+ *      longctx/inference/landmark_cache.py:24-31): mode 1 ('b') = the
+ *      retrieve_k nearest members to target_pose12 (exact ties: lower bank index
+ *      first), returned as ascending bank indices; mode 0 ('a') = all members.
+ * Poses are 12 doubles: R row-major (9) then t (3), in DEVICE memory. */
+int rw_bank_step(rw_bank_state_t* state, int K, int protect_n, int admit, const double* admit_pose12,
+                 int admit_born, int admit_slot, const double* target_pose12, int retrieve_k, int mode,
+                 rw_bank_result_t* result, void* stream);
+
+/* Ulysses layout transforms around the all-to-all (wan_5b/distributed/util.py:52-64
+ * all_to_all with scatter_dim=2/gather_dim=1 and the inverse; ulysses.py:17-55).
+ * pack:   src [B, Ls, H, D] (this rank's sequence shard, all heads) ->
+ *         dst [P][B][Ls][H/P][D] (contiguous block per destination rank).
+ * unpack: src [P][B][Ls][H/P][D] (block from each source rank = its head group)
+ *         -> dst [B, Ls, H, D].
+ * bf16 elements, contiguous src/dst. */
+int rw_a2a_pack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
+int rw_a2a_unpack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
+
+/* Human-readable text of an RW_ERR_* code. */
+const char* rw_error_string(int code);
+
+/* ABI version of this library (incremented on signature changes). */
+int rw_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REWORLD_B200_H */

@@ -1,0 +1,481 @@
+// Chunk attention forward for sm_100a: o = softmax(q k^T * scale) v, non-causal,
+// bf16 in/out, fp32 accumulation in tensor memory.
+//
+// Replaces the reference's attention call for the cached chunk
+// (wan_5b/modules/action_model.py:302 -> wan_5b/modules/attention.py:133-179):
+// the current chunk's queries attend every key of kv_cache[:, :local_end]
+// (sink + recent + retrieved landmarks + the chunk itself), no mask, default
+// scale head_dim^-1/2.  Optionally the 3-D RoPE (+ PM-RoPE phase) of
+// causal_model.py:156-184 / action_model.py:40-51 is applied to q in shared
+// memory before the first QK^T, so raw (normed, un-roped) q can be passed.
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and streams all key
+// tiles of 128 keys through a 5-slot shared-memory ring:
+//   warps 0-3  softmax + epilogue of query tile 0   (one query row per thread)
+//   warps 4-7  softmax + epilogue of query tile 1
+//   warp  8    TMA producer (Q tiles, then K_j, V_j into the ring)
+//   warp  9    tcgen05.mma issuer + TMEM owner
+//   warps 10-11 idle
+// Tensor memory (512 columns x 128 lanes, fp32):
+//   S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512);  P_i (bf16 pairs)
+//   overwrites the first 64 columns of S_i once S_i has been read.
+// MMA order per key tile j (single issuing thread, executed in order):
+//   PV0(j-1), QK0(j), PV1(j-1), QK1(j)
+// so that P_i(j-1) is consumed before S_i(j) overwrites it, and the commit that
+// publishes S_i(j) also guarantees PV_i(j-1) has landed in O_i; the softmax
+// warps can therefore rescale O_i in place between S_i(j) ready and P_i(j)
+// published.  Rescaling is skipped unless the running row maximum grew by more
+// than 2^8 in the exponent (the exponent base stays stale otherwise, which is
+// exact after the final division by the row sum).
+#include "common.cuh"
+#include "host_util.h"
+
+namespace rw {
+namespace attn {
+
+constexpr int BM = 128;                     // query rows per tile
+constexpr int BN = 128;                     // keys per tile
+constexpr int HD = 128;                     // head dim
+constexpr int NSLOT = 5;                    // K/V ring slots (K_j and V_j alternate)
+constexpr int TILE_BYTES = BM * HD * 2;     // 32 KB: every Q/K/V/O tile
+constexpr int HALF_BYTES = TILE_BYTES / 2;  // 128 rows x 64 columns (one TMA box)
+constexpr int NUM_THREADS = 384;
+constexpr int SMEM_BYTES = (2 + NSLOT) * TILE_BYTES + 1024;  // + 1 KB to align to the swizzle atom
+__host__ __device__ constexpr uint32_t tcol_s(int i) { return (uint32_t)i * 128u; }        // S_i columns
+__host__ __device__ constexpr uint32_t tcol_o(int i) { return 256u + (uint32_t)i * 128u; } // O_i columns
+constexpr int WARP_LOAD = 8;
+constexpr int WARP_MMA = 9;
+constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
+
+struct Params {
+  int B, Lq, Lk, H;
+  float scale_log2;
+  int rope_on;
+  rw_rope_t rope;
+  int* status;
+};
+
+struct __align__(8) Barriers {
+  uint64_t slot_full[NSLOT];
+  uint64_t slot_empty[NSLOT];
+  uint64_t q_full[2];
+  uint64_t q_ready[2];
+  uint64_t s_full[2];
+  uint64_t p_ready[2];
+  uint64_t o_done[2];
+  uint64_t epi[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Applies RoPE (+ PM-RoPE phase) in place to one 128-wide row of a
+// 128-byte-swizzled Q tile.  fp64 rotation, rounded to bf16 through fp32 (the
+// reference's complex128 product followed by .type_as(bf16)); the optional
+// phase is applied in fp32 without contraction and rounded again.
+__device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int token, int b, const rw_rope_t& rp) {
+  const int hw = rp.grid_h * rp.grid_w;
+  if (token >= rp.grid_f * hw) return;
+  const int f = token / hw;
+  const int rem = token - f * hw;
+  const int hh = rem / rp.grid_w;
+  const int ww = rem - hh * rp.grid_w;
+  const double2* tab = reinterpret_cast<const double2*>(rp.freqs);
+  const double2* ft = tab + (size_t)(rp.start_frame + f) * 64;
+  const double2* fh = tab + (size_t)hh * 64;
+  const double2* fw = tab + (size_t)ww * 64;
+  const float2* dl =
+      rp.delta_cs ? reinterpret_cast<const float2*>(rp.delta_cs) + ((size_t)b * rp.grid_f + f) * 64 : nullptr;
+  const int e_t = rp.c_t, e_h = rp.c_t + rp.c_h;
+#pragma unroll 1
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const int half = c16 >> 3, c = c16 & 7;
+    uint4* p = reinterpret_cast<uint4*>(tile + half * HALF_BYTES + r * 128 + ((c ^ (r & 7)) << 4));
+    uint4 v = *p;
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = c16 * 4 + e;
+      const double2 cs = (j < e_t) ? ft[j] : ((j < e_h) ? fh[j] : fw[j]);
+      const double xr = (double)bf16_lo(w[e]);
+      const double xi = (double)bf16_hi(w[e]);
+      const double yr = __dsub_rn(__dmul_rn(xr, cs.x), __dmul_rn(xi, cs.y));
+      const double yi = __dadd_rn(__dmul_rn(xr, cs.y), __dmul_rn(xi, cs.x));
+      uint32_t o = pack_bf16x2(__double2float_rn(yr), __double2float_rn(yi));
+      if (dl != nullptr) {
+        const float2 d = dl[j];
+        const float ar = bf16_lo(o), ai = bf16_hi(o);
+        const float zr = __fsub_rn(__fmul_rn(ar, d.x), __fmul_rn(ai, d.y));
+        const float zi = __fadd_rn(__fmul_rn(ar, d.y), __fmul_rn(ai, d.x));
+        o = pack_bf16x2(zr, zi);
+      }
+      w[e] = o;
+    }
+    *p = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Warp-uniform bounded wait.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Barriers& sb, int* status, int err) {
+  const bool ok = mbar_wait(bar, parity, &sb.abort_flag, status, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    const __grid_constant__ Params p) {
+  extern __shared__ uint8_t dsmem_raw[];
+  __shared__ Barriers sb;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_q[2] = {smem, smem + TILE_BYTES};
+  uint8_t* smem_ring = smem + 2 * TILE_BYTES;
+
+  const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int bidx = blockIdx.z;
+  const int q_row0 = blockIdx.x * (2 * BM);
+  const bool has_q1 = (q_row0 + BM) < p.Lq;
+  const int n_kv = (p.Lk + BN - 1) / BN;
+  const int kv_tail = p.Lk - (n_kv - 1) * BN;  // valid keys in the last tile, 1..128
+
+  if (threadIdx.x == WARP_LOAD * 32) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&sb.slot_full[s], 1);
+      mbar_init(&sb.slot_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sb.q_full[i], 1);
+      mbar_init(&sb.q_ready[i], BM);
+      mbar_init(&sb.s_full[i], 1);
+      mbar_init(&sb.p_ready[i], BM);
+      mbar_init(&sb.o_done[i], 1);
+      mbar_init(&sb.epi[i], BM);
+    }
+    mbar_init(&sb.drain, 1);
+    sb.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc(&sb.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+
+  if (warp == WARP_LOAD) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      const uint64_t pol = l2_policy_evict_last();  // K/V tiles are re-read by the other query CTAs of the head
+      mbar_expect_tx(&sb.q_full[0], TILE_BYTES);
+      tma_load_4d(smem_q[0], &tm_q, &sb.q_full[0], 0, head, q_row0, bidx);
+      tma_load_4d(smem_q[0] + HALF_BYTES, &tm_q, &sb.q_full[0], 64, head, q_row0, bidx);
+      if (has_q1) {
+        mbar_expect_tx(&sb.q_full[1], TILE_BYTES);
+        tma_load_4d(smem_q[1], &tm_q, &sb.q_full[1], 0, head, q_row0 + BM, bidx);
+        tma_load_4d(smem_q[1] + HALF_BYTES, &tm_q, &sb.q_full[1], 64, head, q_row0 + BM, bidx);
+      }
+      uint32_t g = 0;  // ring uses issued
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t s = g % NSLOT, use = g / NSLOT;
+          if (!mbar_wait(&sb.slot_empty[s], (use & 1) ^ 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_LOAD)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem_ring + s * TILE_BYTES;
+          const CUtensorMap* m = t == 0 ? &tm_k : &tm_v;
+          mbar_expect_tx(&sb.slot_full[s], TILE_BYTES);
+          tma_load_4d_hint(dst, m, &sb.slot_full[s], 0, head, j * BN, bidx, pol);
+          tma_load_4d_hint(dst + HALF_BYTES, m, &sb.slot_full[s], 64, head, j * BN, bidx, pol);
+          ++g;
+        }
+      }
+      // Every issued copy must land before the CTA may exit (normal path: already consumed).
+      const uint32_t first = g > (uint32_t)NSLOT ? g - NSLOT : 0;
+      for (uint32_t u = first; u < g; ++u) mbar_wait_drain(&sb.slot_full[u % NSLOT], (u / NSLOT) & 1);
+      mbar_wait_drain(&sb.q_full[0], 0);
+      if (has_q1) mbar_wait_drain(&sb.q_full[1], 0);
+    }
+    __syncwarp();
+  } else if (warp == WARP_MMA) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, HD, 0, 1);  // P from TMEM, V MN-major
+      const uint32_t q_addr[2] = {smem_u32(smem_q[0]), smem_u32(smem_q[1])};
+      const uint32_t ring_addr = smem_u32(smem_ring);
+      bool ok = mbar_wait(&sb.q_ready[0], 0, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
+      if (ok && has_q1) ok = mbar_wait(&sb.q_ready[1], 0, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
+      tc_fence_after();
+
+      auto issue_qk = [&](int i, uint32_t k_addr) {
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+          const uint64_t da = umma_desc(q_addr[i] + off, 16, 1024);
+          const uint64_t db = umma_desc(k_addr + off, 16, 1024);
+          mma_ss(tmem + tcol_s(i), da, db, IDESC_QK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int i, uint32_t v_addr, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t db = umma_desc(v_addr + kk * 2048, HALF_BYTES, 1024);
+          mma_ts(tmem + tcol_o(i), tmem + tcol_s(i) + kk * 8, db, IDESC_PV, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+
+      uint32_t g = 0;
+      uint32_t v_prev_slot = 0, v_prev_par = 0;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const uint32_t sK = g % NSLOT, parK = (g / NSLOT) & 1;
+        ++g;
+        const uint32_t sV = g % NSLOT, parV = (g / NSLOT) & 1;
+        ++g;
+        if (!(ok = mbar_wait(&sb.slot_full[sK], parK, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
+        const uint32_t k_addr = ring_addr + sK * TILE_BYTES;
+        const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
+        if (j > 0) {
+          if (!(ok = mbar_wait(&sb.p_ready[0], (j - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
+          if (!(ok = mbar_wait(&sb.slot_full[v_prev_slot], v_prev_par, &sb.abort_flag, p.status,
+                               RW_STATUS_TIMEOUT_MMA)))
+            break;
+          tc_fence_after();
+          issue_pv(0, vp_addr, j > 1);
+        }
+        issue_qk(0, k_addr);
+        tc_commit(&sb.s_full[0]);
+        if (has_q1) {
+          if (j > 0) {
+            if (!(ok = mbar_wait(&sb.p_ready[1], (j - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA)))
+              break;
+            tc_fence_after();
+            issue_pv(1, vp_addr, j > 1);
+          }
+          issue_qk(1, k_addr);
+          tc_commit(&sb.s_full[1]);
+        }
+        if (j > 0) tc_commit(&sb.slot_empty[v_prev_slot]);
+        tc_commit(&sb.slot_empty[sK]);
+        v_prev_slot = sV;
+        v_prev_par = parV;
+      }
+      if (ok) {
+        const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
+        ok = mbar_wait(&sb.p_ready[0], (n_kv - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA) &&
+             mbar_wait(&sb.slot_full[v_prev_slot], v_prev_par, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
+        if (ok) {
+          tc_fence_after();
+          issue_pv(0, vp_addr, n_kv > 1);
+          tc_commit(&sb.o_done[0]);
+          if (has_q1) {
+            ok = mbar_wait(&sb.p_ready[1], (n_kv - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
+            if (ok) {
+              tc_fence_after();
+              issue_pv(1, vp_addr, n_kv > 1);
+              tc_commit(&sb.o_done[1]);
+            }
+          }
+          tc_commit(&sb.slot_empty[v_prev_slot]);
+        }
+      }
+      // All MMAs issued by this thread complete before teardown.
+      tc_commit(&sb.drain);
+      mbar_wait_drain(&sb.drain, 0);
+    }
+    __syncwarp();
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int i = warp >> 2;  // query tile of this warpgroup
+    const int r = threadIdx.x & 127;
+    const bool active = (i == 0) || has_q1;
+    if (active) {
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t tS = tmem + lane_base + tcol_s(i);
+      const uint32_t tO = tmem + lane_base + tcol_o(i);
+      const float sl2 = p.scale_log2;
+      const int row0 = q_row0 + i * BM;
+      bool ok = warp_wait(&sb.q_full[i], 0, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX);
+      if (ok) {
+        if (p.rope_on) rope_row_inplace(smem_q[i], r, row0 + r, bidx, p.rope);
+        fence_proxy_async_smem();
+        mbar_arrive(&sb.q_ready[i]);
+      }
+      float m_used = -INFINITY;
+      float l_part[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (!(ok = warp_wait(&sb.s_full[i], j & 1, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX))) break;
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, sr[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) reg_fence32(sr[c]);
+        if (j == n_kv - 1 && kv_tail < BN) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
+        }
+        float mx[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(sr[q >> 1][(q & 1) * 16]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = (c * 2) + (e >> 4);
+            mx[q] = fmaxf(mx[q], __uint_as_float(sr[c][e]));
+          }
+        const float row_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        const float m_new = fmaxf(m_used, row_max);
+        const bool need = (m_new - m_used) * sl2 > RESCALE_THRESHOLD;
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2((m_used - m_new) * sl2);
+          m_used = m_new;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) l_part[q] *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // O_i is quiescent here: PV_i(j-1) completed before S_i(j) was published.
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+        const float nm = -m_used * sl2;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = 64 * h + 2 * e;
+            const float s0 = __uint_as_float(sr[col >> 5][col & 31]);
+            const float s1 = __uint_as_float(sr[(col + 1) >> 5][(col + 1) & 31]);
+            const float p0 = fast_exp2(fmaf(s0, sl2, nm));
+            const float p1 = fast_exp2(fmaf(s1, sl2, nm));
+            l_part[e & 3] += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(tS + 32 * h, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&sb.p_ready[i]);
+      }
+      // ---- epilogue: O_i / l -> bf16 -> smem (reusing Q_i) -> TMA store
+      if (ok) ok = warp_wait(&sb.o_done[i], 0, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX);
+      if (ok) {
+        tc_fence_after();
+        const float l = (l_part[0] + l_part[1]) + (l_part[2] + l_part[3]);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint8_t* out = smem_q[i];
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+          const int half = c >> 1;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = (c & 1) * 4 + q;
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(out + half * HALF_BYTES + r * 128 + ((chunk ^ (r & 7)) << 4)) = v;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&sb.epi[i]);
+        if (r == 0) {
+          if (mbar_wait(&sb.epi[i], 0, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_SOFTMAX)) {
+            tma_store_4d(&tm_o, out, 0, head, row0, bidx);
+            tma_store_4d(&tm_o, out + HALF_BYTES, 64, head, row0, bidx);
+            bulk_commit_group();
+            bulk_wait_group_read<0>();
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace rw
+
+using namespace rw;
+
+extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H,
+                           int D, long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl,
+                           long long k_sh, long long v_sb, long long v_sl, long long v_sh, long long o_sb,
+                           long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope, int* status,
+                           void* stream) {
+  if (!q || !k || !v || !o) return RW_ERR_INVALID_ARG;
+  if (D != attn::HD) return RW_ERR_UNSUPPORTED;
+  if (B < 1 || Lq < 1 || Lk < 1 || H < 1 || B > 65535 || H > 65535) return RW_ERR_INVALID_ARG;
+  if (!(softmax_scale > 0.f)) return RW_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return RW_ERR_INVALID_ARG;
+  const long long strides[12] = {q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb, o_sl, o_sh};
+  for (int i = 0; i < 12; ++i) {
+    const bool batch_stride = (i % 3) == 0;
+    if (batch_stride && B == 1) continue;
+    if (!stride_ok(strides[i])) return RW_ERR_INVALID_ARG;
+  }
+  attn::Params prm{};
+  prm.B = B;
+  prm.Lq = Lq;
+  prm.Lk = Lk;
+  prm.H = H;
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  prm.status = status;
+  prm.rope_on = 0;
+  if (rope != nullptr) {
+    const rw_rope_t& r = *rope;
+    if (!r.freqs || r.c_t + r.c_h + r.c_w != D / 2 || r.grid_f < 1 || r.grid_h < 1 || r.grid_w < 1 ||
+        r.start_frame < 0 || r.start_frame + r.grid_f > r.max_pos || r.grid_h > r.max_pos || r.grid_w > r.max_pos)
+      return RW_ERR_INVALID_ARG;
+    prm.rope = r;
+    prm.rope_on = 1;
+  }
+  CUtensorMap mq, mk, mv, mo;
+  if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, D, q_sb, q_sl, q_sh, attn::BM) ||
+      make_bf16_bl_hd_map(&mk, k, B, Lk, H, D, k_sb, k_sl, k_sh, attn::BN) ||
+      make_bf16_bl_hd_map(&mv, v, B, Lk, H, D, v_sb, v_sl, v_sh, attn::BN) ||
+      make_bf16_bl_hd_map(&mo, o, B, Lq, H, D, o_sb, o_sl, o_sh, attn::BM))
+    return RW_ERR_DRIVER;
+  static unsigned long long attr_done = 0;
+  if (!ensure_smem_attr((const void*)attn::attn_fwd_kernel, attn::SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
+  dim3 grid((Lq + 2 * attn::BM - 1) / (2 * attn::BM), H, B);
+  attn::attn_fwd_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(mq, mk, mv, mo, prm);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}
