@@ -99,18 +99,33 @@ typedef struct rw_copy_desc {
  * overlap each other's destinations.  Bit-exact byte copies. */
 int rw_copy_chunks(const rw_copy_desc_t* descs, int n, int* status, void* stream);
 
-/* Landmark-bank decision state in device memory (all fields written only by
- * rw_bank_step; zero-initialise before the first call).  Capacity RW_BANK_MAX. */
+/* A camera pose as the landmark bank scores it (8 doubles).  The host fills it
+ * from the 4x4 pose the reference passes around:
+ *   t        = pose[:3, 3]
+ *   yaw_r    = math.degrees(math.atan2(pose[0,2], pose[2,2]))      (retrieval,
+ *              longctx/inference/landmark_cache.py:27-28)
+ *   yaw_e    = np.degrees(np.arctan2(pose[0,2], pose[2,2])) in fp64  (eviction,
+ *              longctx/inference/landmark_cache_v2.py:93-94; numpy's arctan2 and
+ *              Python's atan2 differ in the last bit for some inputs)
+ *   is_f32   = 1.0 when the pose array is float32 (the pipeline's chunk poses,
+ *              pipeline/causal_diffusion_inference_compressed.py:374-377): then
+ *              retrieval forms the translation difference and its norm in fp32
+ *              as numpy does for float32 arrays, else in fp64. */
+typedef struct rw_pose {
+  double tx, ty, tz, yaw_r, yaw_e, is_f32, pad0, pad1;
+} rw_pose_t;
+
+/* Landmark-bank decision state in device memory (written only by rw_bank_step;
+ * zero-initialise before the first call).  Capacity RW_BANK_MAX members. */
 #define RW_BANK_MAX 1024
 typedef struct rw_bank_state {
   int n;          /* members in the bank (list order = admission order minus evictions) */
   int admitted;   /* members ever admitted (drives protect-earliest-n) */
   int pad[2];
-  double tx[RW_BANK_MAX], ty[RW_BANK_MAX], tz[RW_BANK_MAX]; /* translation of each member's pose */
-  double yaw[RW_BANK_MAX];                                  /* degrees(atan2(R02, R22)) */
+  rw_pose_t pose[RW_BANK_MAX];
   int born[RW_BANK_MAX];
-  int slot[RW_BANK_MAX];                                    /* caller's storage slot of the member */
-  int prot[RW_BANK_MAX];                                    /* 1 = protected from eviction */
+  int slot[RW_BANK_MAX];  /* caller's storage slot of the member */
+  int prot[RW_BANK_MAX];  /* 1 = protected from eviction */
 } rw_bank_state_t;
 
 /* Result of one rw_bank_step (device memory). */
@@ -120,23 +135,25 @@ typedef struct rw_bank_result {
   int evicted_slot[4];
   int n_bank;          /* bank size after the step */
   int nR;              /* number of retrieved members */
+  int pad;
   int R[RW_BANK_MAX];  /* retrieved bank-list indices, ascending */
   int R_slot[RW_BANK_MAX];
 } rw_bank_result_t;
 
-/* One bank decision, single warp-level kernel, fp64:
- *  (1) when admit != 0: while the bank holds >= K members evict the member
- *      chosen by landmark_cache_v2.py:465-479 (_evict_index: protect the first
- *      protect_n admitted, else smallest nearest-neighbour pose distance, ties
- *      evict the later-born), then append {admit_pose12, admit_born,
- *      admit_slot} (:481-495 _bank_insert, always-admit);
+/* One bank decision, one launch of a single-CTA kernel, fp64:
+ *  (1) when admit != 0: while the bank holds >= K members, evict the member
+ *      chosen by landmark_cache_v2.py:465-479 (_evict_index: the first
+ *      protect_n admitted are exempt, otherwise the smallest nearest-neighbour
+ *      pose distance of _bank_D :90-98, ties evict the later-born), then append
+ *      {admit_pose, admit_born, admit_slot} (:481-495 _bank_insert, always-admit);
  *  (2) retrieval (:538-592 _retrieve, plain top-k by pose_dist of
- *      longctx/inference/landmark_cache.py:24-31): mode 1 ('b') = the
- *      retrieve_k nearest members to target_pose12 (exact ties: lower bank index
- *      first), returned as ascending bank indices; mode 0 ('a') = all members.
- * Poses are 12 doubles: R row-major (9) then t (3), in DEVICE memory. */
-int rw_bank_step(rw_bank_state_t* state, int K, int protect_n, int admit, const double* admit_pose12,
-                 int admit_born, int admit_slot, const double* target_pose12, int retrieve_k, int mode,
+ *      landmark_cache.py:24-31) with warp-level top-k selection: mode 1 ('b') =
+ *      the retrieve_k members nearest to *target (exact distance ties: lower
+ *      bank index first), returned as ascending bank indices; mode 0 ('a') =
+ *      all members.  target may be NULL in mode 0.
+ * Poses, state and result live in DEVICE memory. */
+int rw_bank_step(rw_bank_state_t* state, int K, int protect_n, int admit, const rw_pose_t* admit_pose,
+                 int admit_born, int admit_slot, const rw_pose_t* target, int retrieve_k, int mode,
                  rw_bank_result_t* result, void* stream);
 
 /* Ulysses layout transforms around the all-to-all (wan_5b/distributed/util.py:52-64

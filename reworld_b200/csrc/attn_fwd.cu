@@ -29,6 +29,7 @@
 // exact after the final division by the row sum).
 #include "common.cuh"
 #include "host_util.h"
+#include "rope.cuh"
 
 namespace rw {
 namespace attn {
@@ -70,48 +71,15 @@ struct __align__(8) Barriers {
 };
 
 // Applies RoPE (+ PM-RoPE phase) in place to one 128-wide row of a
-// 128-byte-swizzled Q tile.  fp64 rotation, rounded to bf16 through fp32 (the
-// reference's complex128 product followed by .type_as(bf16)); the optional
-// phase is applied in fp32 without contraction and rounded again.
+// 128-byte-swizzled Q tile (arithmetic of rope.cuh, same as the cache-store kernel).
 __device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int token, int b, const rw_rope_t& rp) {
-  const int hw = rp.grid_h * rp.grid_w;
-  if (token >= rp.grid_f * hw) return;
-  const int f = token / hw;
-  const int rem = token - f * hw;
-  const int hh = rem / rp.grid_w;
-  const int ww = rem - hh * rp.grid_w;
-  const double2* tab = reinterpret_cast<const double2*>(rp.freqs);
-  const double2* ft = tab + (size_t)(rp.start_frame + f) * 64;
-  const double2* fh = tab + (size_t)hh * 64;
-  const double2* fw = tab + (size_t)ww * 64;
-  const float2* dl =
-      rp.delta_cs ? reinterpret_cast<const float2*>(rp.delta_cs) + ((size_t)b * rp.grid_f + f) * 64 : nullptr;
-  const int e_t = rp.c_t, e_h = rp.c_t + rp.c_h;
+  const RopeToken rt = rope_token(rp, token, b);
+  if (!rt.on) return;
 #pragma unroll 1
   for (int c16 = 0; c16 < 16; ++c16) {
     const int half = c16 >> 3, c = c16 & 7;
     uint4* p = reinterpret_cast<uint4*>(tile + half * HALF_BYTES + r * 128 + ((c ^ (r & 7)) << 4));
-    uint4 v = *p;
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int j = c16 * 4 + e;
-      const double2 cs = (j < e_t) ? ft[j] : ((j < e_h) ? fh[j] : fw[j]);
-      const double xr = (double)bf16_lo(w[e]);
-      const double xi = (double)bf16_hi(w[e]);
-      const double yr = __dsub_rn(__dmul_rn(xr, cs.x), __dmul_rn(xi, cs.y));
-      const double yi = __dadd_rn(__dmul_rn(xr, cs.y), __dmul_rn(xi, cs.x));
-      uint32_t o = pack_bf16x2(__double2float_rn(yr), __double2float_rn(yi));
-      if (dl != nullptr) {
-        const float2 d = dl[j];
-        const float ar = bf16_lo(o), ai = bf16_hi(o);
-        const float zr = __fsub_rn(__fmul_rn(ar, d.x), __fmul_rn(ai, d.y));
-        const float zi = __fadd_rn(__fmul_rn(ar, d.y), __fmul_rn(ai, d.x));
-        o = pack_bf16x2(zr, zi);
-      }
-      w[e] = o;
-    }
-    *p = make_uint4(w[0], w[1], w[2], w[3]);
+    *p = rope_chunk(*p, c16, rt);
   }
 }
 
@@ -460,11 +428,8 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
   prm.status = status;
   prm.rope_on = 0;
   if (rope != nullptr) {
-    const rw_rope_t& r = *rope;
-    if (!r.freqs || r.c_t + r.c_h + r.c_w != D / 2 || r.grid_f < 1 || r.grid_h < 1 || r.grid_w < 1 ||
-        r.start_frame < 0 || r.start_frame + r.grid_f > r.max_pos || r.grid_h > r.max_pos || r.grid_w > r.max_pos)
-      return RW_ERR_INVALID_ARG;
-    prm.rope = r;
+    if (!rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
+    prm.rope = *rope;
     prm.rope_on = 1;
   }
   CUtensorMap mq, mk, mv, mo;

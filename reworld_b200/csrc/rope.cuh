@@ -1,0 +1,83 @@
+// 3-D RoPE (+ PM-RoPE phase) arithmetic shared by the attention prologue and
+// the cache-store kernel.
+//
+// Reference: causal_rope_apply (wan_5b/modules/causal_model.py:156-184) rotates
+// complex pair j of token t by freqs[start_frame + f][j] (j < c_t),
+// freqs[h][j] (c_t <= j < c_t + c_h) or freqs[w][j] (otherwise), with
+// (f, h, w) the token's grid position, as a complex128 product, then casts to
+// bf16 (.type_as); pm_rope_delta_apply (action_model.py:40-51) then multiplies
+// by e^{i delta} in complex64 and casts to bf16 again.  The complex products
+// use separately rounded multiplies and adds (no fused multiply-add), the
+// double -> bf16 cast rounds through fp32, as the reference's CPU kernels do.
+#pragma once
+
+#include "common.cuh"
+
+namespace rw {
+
+struct RopeToken {
+  const double2* ft;  // freqs row of the temporal position
+  const double2* fh;  // freqs row of the height position
+  const double2* fw;  // freqs row of the width position
+  const float2* dl;   // PM-RoPE (cos, sin) row of the frame, or null
+  int e_t, e_h;       // pair index where the h and w sections start
+  bool on;            // false: token is past f*h*w and stays unchanged
+};
+
+__device__ __forceinline__ RopeToken rope_token(const rw_rope_t& rp, int token, int b) {
+  RopeToken rt;
+  const int hw = rp.grid_h * rp.grid_w;
+  rt.on = token < rp.grid_f * hw;
+  const int tok = rt.on ? token : 0;
+  const int f = tok / hw;
+  const int rem = tok - f * hw;
+  const int hh = rem / rp.grid_w;
+  const int ww = rem - hh * rp.grid_w;
+  const double2* tab = reinterpret_cast<const double2*>(rp.freqs);
+  rt.ft = tab + (size_t)(rp.start_frame + f) * 64;
+  rt.fh = tab + (size_t)hh * 64;
+  rt.fw = tab + (size_t)ww * 64;
+  rt.dl = rp.delta_cs ? reinterpret_cast<const float2*>(rp.delta_cs) + ((size_t)b * rp.grid_f + f) * 64 : nullptr;
+  rt.e_t = rp.c_t;
+  rt.e_h = rp.c_t + rp.c_h;
+  return rt;
+}
+
+// Rotates one packed bf16 pair (low half = real, high half = imaginary) that is
+// complex pair j of the token.
+__device__ __forceinline__ uint32_t rope_pair(uint32_t w, int j, const RopeToken& rt) {
+  const double2 cs = (j < rt.e_t) ? rt.ft[j] : ((j < rt.e_h) ? rt.fh[j] : rt.fw[j]);
+  const double xr = (double)bf16_lo(w);
+  const double xi = (double)bf16_hi(w);
+  const double yr = __dsub_rn(__dmul_rn(xr, cs.x), __dmul_rn(xi, cs.y));
+  const double yi = __dadd_rn(__dmul_rn(xr, cs.y), __dmul_rn(xi, cs.x));
+  uint32_t o = pack_bf16x2(__double2float_rn(yr), __double2float_rn(yi));
+  if (rt.dl != nullptr) {
+    const float2 d = rt.dl[j];
+    const float ar = bf16_lo(o), ai = bf16_hi(o);
+    const float zr = __fsub_rn(__fmul_rn(ar, d.x), __fmul_rn(ai, d.y));
+    const float zi = __fadd_rn(__fmul_rn(ar, d.y), __fmul_rn(ai, d.x));
+    o = pack_bf16x2(zr, zi);
+  }
+  return o;
+}
+
+// Rotates 4 consecutive pairs (one 16-byte chunk: elements 8*c16 .. 8*c16+7).
+__device__ __forceinline__ uint4 rope_chunk(uint4 v, int c16, const RopeToken& rt) {
+  if (!rt.on) return v;
+  v.x = rope_pair(v.x, 4 * c16 + 0, rt);
+  v.y = rope_pair(v.y, 4 * c16 + 1, rt);
+  v.z = rope_pair(v.z, 4 * c16 + 2, rt);
+  v.w = rope_pair(v.w, 4 * c16 + 3, rt);
+  return v;
+}
+
+// Host-side validation of a rope descriptor for head_dim D.
+inline bool rope_args_ok(const rw_rope_t& r, int D) {
+  return r.freqs != nullptr && r.c_t >= 0 && r.c_h >= 0 && r.c_w >= 0 && r.c_t + r.c_h + r.c_w == D / 2 &&
+         r.grid_f >= 1 && r.grid_h >= 1 && r.grid_w >= 1 && r.start_frame >= 0 &&
+         r.start_frame + r.grid_f <= r.max_pos && r.grid_h <= r.max_pos && r.grid_w <= r.max_pos &&
+         (reinterpret_cast<uintptr_t>(r.freqs) & 15u) == 0 && (reinterpret_cast<uintptr_t>(r.delta_cs) & 7u) == 0;
+}
+
+}  // namespace rw

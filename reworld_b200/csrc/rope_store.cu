@@ -1,0 +1,122 @@
+// RoPE (+ PM-RoPE phase) on the new chunk's K and the KV-cache write of K and V.
+//
+// Replaces wan_5b/modules/action_model.py:265-292: q_f, k_f = apply_rope(q, k,
+// delta_tok, start_f=g_start_f, ...) followed by
+// kv_cache["k"][:, local_start:local_end] = k_f and kv_cache["v"][...] = v.
+// One thread per 16-byte chunk (8 bf16 = 4 complex pairs) of a (batch, token,
+// head) row; V is a plain 16-byte copy.  HBM-bound: reads k, v (and q), writes
+// the cache rows (and roped q).
+#include "common.cuh"
+#include "host_util.h"
+#include "rope.cuh"
+
+namespace rw {
+namespace store {
+
+struct Params {
+  const uint8_t* k;
+  const uint8_t* v;
+  const uint8_t* q_in;
+  uint8_t* q_out;
+  uint8_t* ck;
+  uint8_t* cv;
+  int L, H, dst_start;
+  long long k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, q_sb, q_sl, q_sh, qo_sb, qo_sl, qo_sh;
+  long long ck_sb, ck_sl, ck_sh, cv_sb, cv_sl, cv_sh;
+  int rope_on;
+  rw_rope_t rope;
+};
+
+__device__ __forceinline__ uint4 ldg16(const uint8_t* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void stg16(uint8_t* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
+__global__ void __launch_bounds__(256) rope_kv_store_kernel(const __grid_constant__ Params p) {
+  const long long n = (long long)p.L * p.H * 16;
+  const int b = blockIdx.y;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c16 = (int)(idx & 15);
+    const long long th = idx >> 4;
+    const int h = (int)(th % p.H);
+    const int t = (int)(th / p.H);
+    const long long eoff = (long long)c16 * 8;  // element offset within the head row
+    RopeToken rt;
+    if (p.rope_on) rt = rope_token(p.rope, t, b);
+    // V: plain copy into the cache slot
+    {
+      const uint4 vv = ldg16(p.v + 2 * (b * p.v_sb + t * p.v_sl + h * p.v_sh + eoff));
+      stg16(p.cv + 2 * (b * p.cv_sb + (long long)(p.dst_start + t) * p.cv_sl + h * p.cv_sh + eoff), vv);
+    }
+    // K: rotate, then store into the cache slot
+    {
+      uint4 kv = ldg16(p.k + 2 * (b * p.k_sb + t * p.k_sl + h * p.k_sh + eoff));
+      if (p.rope_on) kv = rope_chunk(kv, c16, rt);
+      stg16(p.ck + 2 * (b * p.ck_sb + (long long)(p.dst_start + t) * p.ck_sl + h * p.ck_sh + eoff), kv);
+    }
+    // Q: optional rotated copy
+    if (p.q_in != nullptr) {
+      uint4 qv = ldg16(p.q_in + 2 * (b * p.q_sb + t * p.q_sl + h * p.q_sh + eoff));
+      if (p.rope_on) qv = rope_chunk(qv, c16, rt);
+      stg16(p.q_out + 2 * (b * p.qo_sb + t * p.qo_sl + h * p.qo_sh + eoff), qv);
+    }
+  }
+}
+
+}  // namespace store
+}  // namespace rw
+
+using namespace rw;
+
+extern "C" int rw_rope_kv_store(const void* k, const void* v, const void* q_in, void* q_out, void* cache_k,
+                                void* cache_v, int B, int L, int H, int D, int dst_start, long long k_sb,
+                                long long k_sl, long long k_sh, long long v_sb, long long v_sl, long long v_sh,
+                                long long q_sb, long long q_sl, long long q_sh, long long qo_sb, long long qo_sl,
+                                long long qo_sh, long long ck_sb, long long ck_sl, long long ck_sh,
+                                long long cv_sb, long long cv_sl, long long cv_sh, const rw_rope_t* rope,
+                                void* stream) {
+  if (!k || !v || !cache_k || !cache_v) return RW_ERR_INVALID_ARG;
+  if ((q_in == nullptr) != (q_out == nullptr)) return RW_ERR_INVALID_ARG;
+  if (D != 128) return RW_ERR_UNSUPPORTED;
+  if (B < 1 || B > 65535 || L < 0 || H < 1 || dst_start < 0) return RW_ERR_INVALID_ARG;
+  if (L == 0) return RW_OK;
+  const void* ptrs[6] = {k, v, q_in, q_out, cache_k, cache_v};
+  for (int i = 0; i < 6; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i])) return RW_ERR_INVALID_ARG;
+  const long long st[18] = {k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, q_sb, q_sl, q_sh,
+                            qo_sb, qo_sl, qo_sh, ck_sb, ck_sl, ck_sh, cv_sb, cv_sl, cv_sh};
+  for (int i = 0; i < 18; ++i) {
+    if (i >= 6 && i < 12 && q_in == nullptr) continue;
+    if ((i % 3) == 0 && B == 1) continue;
+    if (st[i] < 0 || (st[i] % 8) != 0) return RW_ERR_INVALID_ARG;
+  }
+  store::Params p{};
+  p.k = (const uint8_t*)k;
+  p.v = (const uint8_t*)v;
+  p.q_in = (const uint8_t*)q_in;
+  p.q_out = (uint8_t*)q_out;
+  p.ck = (uint8_t*)cache_k;
+  p.cv = (uint8_t*)cache_v;
+  p.L = L;
+  p.H = H;
+  p.dst_start = dst_start;
+  p.k_sb = B == 1 ? 0 : k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
+  p.v_sb = B == 1 ? 0 : v_sb; p.v_sl = v_sl; p.v_sh = v_sh;
+  p.q_sb = B == 1 ? 0 : q_sb; p.q_sl = q_sl; p.q_sh = q_sh;
+  p.qo_sb = B == 1 ? 0 : qo_sb; p.qo_sl = qo_sl; p.qo_sh = qo_sh;
+  p.ck_sb = B == 1 ? 0 : ck_sb; p.ck_sl = ck_sl; p.ck_sh = ck_sh;
+  p.cv_sb = B == 1 ? 0 : cv_sb; p.cv_sl = cv_sl; p.cv_sh = cv_sh;
+  p.rope_on = 0;
+  if (rope != nullptr) {
+    if (!rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
+    p.rope = *rope;
+    p.rope_on = 1;
+  }
+  const long long n = (long long)L * H * 16;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  dim3 grid((unsigned)blocks, B);
+  store::rope_kv_store_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}

@@ -1,0 +1,155 @@
+"""Drop-in forward for the reference's CausalWanPropSelfAttention (inference branch).
+
+`prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask,
+kv_cache=None, current_start=0, cache_start=None, prope_context=None)` has the
+signature and semantics of wan_5b/modules/action_model.py:148-319 with a KV
+cache: q/k/v projections + RMSNorm over all heads, PM-RoPE phase and V-side
+P^-1 residual when prope_context is given, the chunk's RoPE at its start frame
+(or kv_cache["rope_start_frame"]), the cache write at
+[local_end - num_new, local_end), attention over kv_cache[:, :local_end], the
+index updates of :304-305 and the o projection (+ P residual).
+
+What runs on the B200 kernels: the RoPE of k and the cache write of k/v (one
+rw_rope_kv_store launch) and the attention with q's RoPE applied inside the
+kernel (rw_attn_fwd).  The projections, RMSNorm and the PRoPE residual
+matmuls stay torch GPU ops.  The KV cache must be bf16.
+
+Install it per block the way the reference installs its sequence-parallel
+forward (wan_5b/text2video.py:150-154): `install(model)`.
+"""
+import math
+import types
+
+import torch
+
+from .attention import chunk_attention
+from .kv_cache import rope_kv_store
+from .rope import RopeArgs, device_table
+
+
+def _invert_se3(T):
+    R = T[..., :3, :3]
+    t = T[..., :3, 3:]
+    Ri = R.transpose(-1, -2)
+    out = T.clone()
+    out[..., :3, :3] = Ri
+    out[..., :3, 3:] = -Ri @ t
+    out[..., 3, :3] = 0
+    out[..., 3, 3] = 1
+    return out
+
+
+def se3_block_apply(x, prope_context, mode, frame_seqlen):
+    """Block-diagonal 4x4 transform over head_dim per frame (action_model.py:84-114,
+    with its optional translation bound off as by default).  x: [B, L, H, D]."""
+    B, L, H, D = x.shape
+    nf = L // frame_seqlen
+    ctx = prope_context[:, -nf:].to(x.dtype)
+    if mode == "P_inv":
+        ctx = _invert_se3(ctx)
+    xv = x.permute(0, 2, 1, 3).reshape(B, H, nf, frame_seqlen, D // 4, 4)
+    y = torch.matmul(ctx[:, None, :, None, None], xv.unsqueeze(-1)).squeeze(-1)
+    return y.reshape(B, H, L, D).permute(0, 2, 1, 3)
+
+
+def _cache_local_size(local_attn_size):
+    if isinstance(local_attn_size, (list, tuple)):
+        finite = [abs(sz) for sz in local_attn_size if sz != -1]
+        return max(finite) if finite else -1
+    return abs(local_attn_size) if local_attn_size != -1 else -1
+
+
+def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_cache=None, current_start=0,
+                           cache_start=None, prope_context=None):
+    if kv_cache is None:
+        # training / teacher-forcing branch: not part of the cached chunk path
+        return self._rw_reference_forward(x, seq_lens, grid_sizes, freqs, block_mask, kv_cache=kv_cache,
+                                          current_start=current_start, cache_start=cache_start,
+                                          prope_context=prope_context)
+    if kv_cache["k"].dtype != torch.bfloat16:
+        raise NotImplementedError("the B200 chunk-attention path keeps the KV cache in bf16")
+    b, s, n, d = *x.shape[:2], self.num_heads, self.head_dim
+    q = self.norm_q(self.q(x)).view(b, s, n, d)
+    k = self.norm_k(self.k(x)).view(b, s, n, d)
+    v = self.v(x).view(b, s, n, d)
+    g0 = [int(t) for t in grid_sizes[0].tolist()]
+    frame_seqlen = g0[1] * g0[2]
+
+    delta = None
+    if prope_context is not None:
+        R_flat = prope_context[..., :3, :3].flatten(-2)
+        t_vec = prope_context[..., :3, 3]
+        c_all = torch.cat([R_flat, t_vec], dim=-1)
+        T_half = s // frame_seqlen
+        delta = self.pose_mlp(c_all[:, -T_half:])                  # [B, T, d/2] per-frame phase
+        v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen)
+        v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
+
+    num_new = q.shape[1]
+    cur_end = current_start + num_new
+    sink_tokens = self.sink_size * frame_seqlen
+    cache_local = _cache_local_size(self.local_attn_size)
+    self.max_attention_size = None if cache_local == -1 else int(cache_local) * int(frame_seqlen)
+    kv_cache_size = kv_cache["k"].shape[1]
+    g_start_f = current_start // frame_seqlen
+    rsf = kv_cache.get("rope_start_frame") if isinstance(kv_cache, dict) else None
+    if rsf is not None:
+        g_start_f = int(rsf.item())
+    grid = (max(1, num_new // frame_seqlen), g0[1], g0[2])
+
+    global_end = int(kv_cache["global_end_index"].item())
+    local_end_prev = int(kv_cache["local_end_index"].item())
+    if cache_local != -1 and cur_end > global_end and num_new + local_end_prev > kv_cache_size:
+        n_evict = num_new + local_end_prev - kv_cache_size
+        n_roll = local_end_prev - n_evict - sink_tokens
+        for key in ("k", "v"):
+            kv_cache[key][:, sink_tokens:sink_tokens + n_roll] = \
+                kv_cache[key][:, sink_tokens + n_evict:sink_tokens + n_evict + n_roll].clone()
+        local_end = local_end_prev + cur_end - global_end - n_evict
+    else:
+        local_end = local_end_prev + cur_end - global_end
+    local_start = local_end - num_new
+
+    table = device_table(freqs, x.device)
+    rope = RopeArgs(table, grid, g_start_f, head_dim=d, delta=delta)
+    rope_kv_store(k, v, kv_cache["k"], kv_cache["v"], local_start, rope=rope)
+    if self.max_attention_size is None:
+        k_slice = kv_cache["k"][:, :local_end]
+        v_slice = kv_cache["v"][:, :local_end]
+    else:
+        s0 = max(0, local_end - self.max_attention_size)
+        k_slice = kv_cache["k"][:, s0:local_end]
+        v_slice = kv_cache["v"][:, s0:local_end]
+    attn_out = chunk_attention(q, k_slice, v_slice, rope=rope).to(x.dtype)
+    kv_cache["global_end_index"].fill_(cur_end)
+    kv_cache["local_end_index"].fill_(local_end)
+
+    out = self.o(attn_out.flatten(2))
+    if prope_context is not None:
+        x_p = se3_block_apply(attn_out, prope_context, "P", frame_seqlen)
+        out = out + self.prope_proj(x_p.flatten(2))
+    return out
+
+
+def install(model):
+    """Replaces block.self_attn.forward of every block of a CausalWanActionModel
+    (or any module with .blocks[i].self_attn) by prop_self_attn_forward."""
+    blocks = model.blocks if hasattr(model, "blocks") else model
+    n = 0
+    for blk in blocks:
+        sa = blk.self_attn
+        if not hasattr(sa, "_rw_reference_forward"):
+            sa._rw_reference_forward = sa.forward
+        sa.forward = types.MethodType(prop_self_attn_forward, sa)
+        n += 1
+    return n
+
+
+def patch_attention_symbol(module):
+    """Rebinds `module.attention` (e.g. wan_5b.modules.action_model) to this
+    package's attention(), the way the reference's compressed pipeline patches
+    it (pipeline/causal_diffusion_inference_compressed.py:168-214)."""
+    from .attention import attention
+    prev = getattr(module, "attention", None)
+    module.attention = attention
+    return prev

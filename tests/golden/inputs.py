@@ -1,0 +1,112 @@
+"""Seeded inputs of the golden fixtures, shared by make_golden.py (which feeds
+them to the reference) and the tests (which feed them to the oracle and the
+CUDA path).  Everything is drawn from torch CPU generators with fixed seeds;
+each fixture stores a checksum of its inputs so a change of the generator
+stream is caught instead of producing a silent mismatch.
+"""
+import numpy as np
+import torch
+
+ATTN_CASES = [(1, 64, 192, 2), (2, 96, 130, 1), (1, 128, 384, 2), (1, 50, 257, 3)]
+
+SELF_ATTN_DIM, SELF_ATTN_HEADS, HEAD_DIM = 256, 2, 128
+SELF_ATTN_GRID = (3, 4, 5)
+SELF_ATTN_CACHED = 3                       # cached chunks before the new one
+SELF_ATTN_TAGS = (("f32", torch.float32, False), ("f32_ctx", torch.float32, True),
+                  ("bf16", torch.bfloat16, False), ("bf16_ctx", torch.bfloat16, True))
+ROPE_SCALE_H, ROPE_SCALE_W = 12 / 22, 20 / 40   # spatial position interpolation of the 720p config
+
+
+def checksum(*tensors):
+    h = 0.0
+    for t in tensors:
+        a = t.detach().float().cpu().numpy().ravel().astype(np.float64)
+        h += float(np.sum(a * np.cos(np.arange(a.size) * 0.001)))
+    return h
+
+
+def attention_case(i):
+    B, Lq, Lk, H = ATTN_CASES[i]
+    g = torch.Generator().manual_seed(100 + i)
+    q = torch.randn(B, Lq, H, HEAD_DIM, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Lk, H, HEAD_DIM, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Lk, H, HEAD_DIM, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+def rope_case():
+    """x [1, L, 3, 128] bf16 (grid 3x4x5 plus 4 tokens past the grid) and delta [1, L, 1, 64]."""
+    g = torch.Generator().manual_seed(7)
+    f, h, w = 3, 4, 5
+    L = f * h * w + 4
+    x = (torch.randn(1, L, 3, HEAD_DIM, generator=g) * 2.0).to(torch.bfloat16)
+    delta = torch.randn(1, L, 1, HEAD_DIM // 2, generator=g) * 0.5
+    return x, (f, h, w), delta
+
+
+def self_attn_params(param_shapes):
+    """Parameter values in sorted-name order, drawn from one generator (norm weights ~ 1 + N(0, 0.02))."""
+    g = torch.Generator().manual_seed(12)
+    vals = {}
+    for name, shape in sorted(param_shapes.items()):
+        vals[name] = torch.randn(shape, generator=g) * 0.02
+    for nm in ("norm_q.weight", "norm_k.weight"):
+        vals[nm] = 1.0 + torch.randn(param_shapes[nm], generator=g) * 0.02
+    return vals, g
+
+
+def self_attn_inputs(g, dtype, with_ctx):
+    """Cache contents, new-chunk activations and (optionally) the PRoPE context, drawn after the params."""
+    dim, H, d = SELF_ATTN_DIM, SELF_ATTN_HEADS, HEAD_DIM
+    f, h, w = SELF_ATTN_GRID
+    ct = f * h * w
+    n = SELF_ATTN_CACHED * ct
+    k0 = torch.randn(1, n, H, d, generator=g).to(dtype)
+    v0 = torch.randn(1, n, H, d, generator=g).to(dtype)
+    x = torch.randn(1, ct, dim, generator=g).to(dtype)
+    ctx = None
+    if with_ctx:
+        T = SELF_ATTN_CACHED * f + f
+        ang = torch.randn(T, generator=g) * 0.3
+        c, s = torch.cos(ang), torch.sin(ang)
+        P = torch.zeros(1, T, 4, 4)
+        P[0, :, 0, 0], P[0, :, 0, 2], P[0, :, 2, 0], P[0, :, 2, 2] = c, s, -s, c
+        P[0, :, 1, 1] = 1.0
+        P[0, :, 3, 3] = 1.0
+        P[0, :, :3, 3] = torch.randn(T, 3, generator=g) * 0.5
+        ctx = P.to(dtype)
+    return k0, v0, x, ctx
+
+
+def landmark_runs():
+    """name -> (poses, ct, H, D, n_sink, recent_w, K, retrieve_k, mode)."""
+    from reworld_b200.poses import random_walk, yaw_walk
+    return {
+        "walk_cfg2": (random_walk(64, seed=0), 2, 1, 8, 1, 5, 30, 6, "b"),
+        "revisit_cfg4": (random_walk(40, seed=1, revisit_every=8), 2, 1, 8, 1, 5, 30, 6, "b"),
+        "yaw_always_full": (yaw_walk(201, seed=1, step_t=0.25, step_yaw_deg=30.0), 2, 1, 8, 1, 5, 30, 6, "b"),
+        "stress_cfg5": (random_walk(160, seed=5), 2, 1, 8, 1, 7, 120, 16, "b"),
+        "small_k": (yaw_walk(40, seed=3, step_t=0.2, step_yaw_deg=40.0), 3, 2, 8, 1, 3, 8, 3, "b"),
+        "mode_a": (yaw_walk(30, seed=4), 2, 1, 8, 1, 3, 6, 6, "a"),
+    }
+
+
+def landmark_kv(name, c, ct, H, D):
+    """K and V of chunk c of run `name` (bf16 [ct, H, D])."""
+    g = torch.Generator().manual_seed(10_000 * (sorted(landmark_runs_names()).index(name) + 1) + c)
+    k = torch.randn(ct, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(ct, H, D, generator=g).to(torch.bfloat16)
+    return k, v
+
+
+def landmark_runs_names():
+    return ["walk_cfg2", "revisit_cfg4", "yaw_always_full", "stress_cfg5", "small_k", "mode_a"]
+
+
+ULYSSES_SHAPE = (1, 12, 8, 16)   # B, L, H, D
+
+
+def ulysses_shard(rank, world):
+    B, L, H, D = ULYSSES_SHAPE
+    g = torch.Generator().manual_seed(1000 + rank)
+    return torch.randn(B, L // world, H, D, generator=g)

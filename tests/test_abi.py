@@ -1,0 +1,79 @@
+"""The C-ABI library loads and exports every entry point of include/reworld_b200.h;
+argument validation runs on the host (no kernel launch, no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from reworld_b200 import _native
+from reworld_b200.landmark import RwBankResult, RwBankState, RwPose
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _header_functions():
+    src = open(os.path.join(ROOT, "include", "reworld_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(rw_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    declared = _header_functions()
+    assert declared == _native.exported_symbols()
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.rw_abi_version() == _native.ABI_VERSION
+
+
+def test_error_strings():
+    lib = _native.lib()
+    for code in (0, -1, -2, -3, -4, -5, -99):
+        assert isinstance(lib.rw_error_string(code), bytes)
+
+
+def test_struct_sizes_match_header():
+    # rw_pose_t: 8 doubles; state/result sizes follow the header layout
+    assert ctypes.sizeof(RwPose) == 64
+    assert ctypes.sizeof(RwBankState) == 16 + 1024 * 64 + 3 * 1024 * 4
+    assert ctypes.sizeof(RwBankResult) == 48 + 2 * 1024 * 4
+
+
+def test_attn_rejects_bad_arguments_without_launching():
+    lib = _native.lib()
+    args = [None] * 4 + [1, 128, 128, 1, 128] + [0] * 12 + [0.1, None, None, None]
+    assert lib.rw_attn_fwd(*args) == -1                    # null pointers
+    p = ctypes.c_void_p(16)
+    st = [128 * 128, 128, 128] * 4
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 64, *st, 0.1, None, None, None) == -2   # head_dim 64
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 0, 1, 128, *st, 0.1, None, None, None) == -1    # Lk = 0
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *st, -1.0, None, None, None) == -1  # scale <= 0
+    odd = ctypes.c_void_p(18)
+    assert lib.rw_attn_fwd(odd, p, p, p, 1, 128, 128, 1, 128, *st, 0.1, None, None, None) == -1  # misaligned
+    bad = [128 * 128, 130, 128] * 4
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *bad, 0.1, None, None, None) == -1  # stride % 8
+
+
+def test_other_entry_points_reject_bad_arguments():
+    lib = _native.lib()
+    assert lib.rw_copy_chunks(None, 0, None, None) == 0         # nothing to do
+    assert lib.rw_copy_chunks(None, 3, None, None) == -1
+    assert lib.rw_copy_chunks(None, -1, None, None) == -1
+    assert lib.rw_bank_step(None, 30, 2, 0, None, 0, 0, None, 6, 1, None, None) == -1
+    p = ctypes.c_void_p(64)
+    assert lib.rw_bank_step(p, 2000, 2, 0, None, 0, 0, p, 6, 1, p, None) == -1   # K > capacity
+    assert lib.rw_bank_step(p, 30, 2, 1, None, 0, 0, p, 6, 1, p, None) == -1     # admit without pose
+    assert lib.rw_a2a_pack(p, p, 1, 8, 24, 128, 5, None) == -1                 # heads not divisible
+    assert lib.rw_a2a_unpack(None, p, 1, 8, 24, 128, 2, None) == -1
+    z = [0] * 18
+    assert lib.rw_rope_kv_store(p, p, None, None, p, p, 1, 8, 2, 64, 0, *z, None, None) == -2
+    assert lib.rw_rope_kv_store(p, p, p, None, p, p, 1, 8, 2, 128, 0, *z, None, None) == -1
+
+
+def test_import_fails_loudly_without_library(monkeypatch, tmp_path):
+    import reworld_b200.build as b
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "lib_path", lambda: str(tmp_path / "missing.so"))
+    with pytest.raises(ImportError):
+        _native.lib()
