@@ -1,0 +1,504 @@
+"""Benchmark of the per-chunk causal self-attention hot path (704x1280, 12-chunk KV).
+
+One step = one chunk of the streaming rollout through the 30-layer attention
+stack, as the reference's compressed pipeline runs it
+(pipeline/causal_diffusion_inference_compressed.py:621-734 with the shipped
+4-step DMD config): 4 denoising forwards + 1 clean-KV forward, each writing the
+chunk's roped K/V into every layer's cache and attending the chunk's 2640
+queries over the cache (1 sink + 5 recent + 6 retrieved landmarks = 31680 keys)
+plus the chunk itself (34320 keys), then the landmark-bank update: admission
+with eviction, pose top-k retrieval from the 30-entry bank and the gather of
+sink | recent | landmarks into all 30 layers' caches.
+
+value = attention FLOPs of the step (5 x 30 x 4*Lq*Lk*H*D) / step time, whole
+job.  With --gpus N > 1 the step runs Ulysses head-parallel (H/N heads per
+rank, sequence-sharded q/k/v exchanged by NCCL all-to-all, head-resident
+caches and bank), strong scaling.
+
+--impl reference times the reference's own CPU attention path (torch SDPA on
+the host cores, the branch wan_5b/modules/attention.py:164-179 takes without
+flash-attention) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# workload: 704x1280 video, latent 44x80, 2x2 patches -> 22x40 tokens per frame, 3 frames per chunk
+FRAMES, TOK_H, TOK_W = 3, 22, 40
+CT = FRAMES * TOK_H * TOK_W                  # 2640 query tokens per chunk
+N_LAYERS, HEADS, HEAD_DIM = 30, 24, 128
+N_SINK, RECENT_W, N_LANDMARK, BANK_K = 1, 5, 6, 30
+BUDGET = N_SINK + RECENT_W + N_LANDMARK      # 12 chunks
+LK = (BUDGET + 1) * CT                       # 34320 keys (cache + the chunk itself)
+FORWARDS_PER_CHUNK = 5                       # 4 denoise + 1 clean-KV forward
+METRIC = "causal chunk-attn TFLOP/s + ms/chunk, 704x1280 12-chunk KV, 1/2/4/8 B200"
+WORKLOAD = ("704x1280 chunk (3 latent frames, 2640 tokens) x 30 layers x 24 heads x 128, KV budget 12 chunks "
+            "(1 sink + 5 recent + 6 landmarks = 31680 keys) + the chunk itself = 34320 keys; 5 forwards/chunk "
+            "(4 denoise + 1 clean-KV); bank of 30 with pose top-6 retrieval and all-layer gather per chunk")
+
+
+def attn_flops(lq, lk, h):
+    return 4.0 * lq * lk * h * HEAD_DIM
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), \
+            "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "attn_fwd_ncu.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ GPU arm
+class Rollout:
+    """Device state of the rollout on one rank: per-layer caches for this rank's
+    heads, the landmark bank stack, the chunk inputs."""
+
+    def __init__(self, device, heads, seq_shard, world, rank, group):
+        from reworld_b200 import RopeArgs, build_freqs, device_table
+        from reworld_b200.landmark import LandmarkBankStack
+        from reworld_b200.poses import random_walk
+        self.dev, self.H, self.world, self.rank, self.group = device, heads, world, rank, group
+        self.cap = (BUDGET + 1) * CT
+        g = torch.Generator(device=device).manual_seed(1234 + rank)
+        self.cache_k = [torch.zeros(1, self.cap, heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
+                        for _ in range(N_LAYERS)]
+        self.cache_v = [torch.zeros_like(c) for c in self.cache_k]
+        # activations of the chunk per layer: sequence-sharded when world > 1
+        shape = (1, seq_shard, HEADS, HEAD_DIM)
+        self.q = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
+        self.k = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
+        self.v = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
+        self.out = [torch.empty(1, CT, heads, HEAD_DIM, dtype=torch.bfloat16, device=device) for _ in range(N_LAYERS)]
+        self.bank = LandmarkBankStack(CT, N_LAYERS, heads, HEAD_DIM, n_sink=N_SINK, recent_w=RECENT_W, K=BANK_K,
+                                      retrieve_k=N_LANDMARK, mode="b", device=device)
+        self.table = device_table(build_freqs(HEAD_DIM, 12 / 22, 20 / 40), device)
+        self.RopeArgs = RopeArgs
+        self.poses = random_walk(4096, seed=0, revisit_every=8)
+        self.chunk = 0
+        self.tot = 0
+        self.launches = 0
+        self.attn_events = []
+
+    def fill_bank(self, n_chunks):
+        """Cold-start the cache: run the bank update for n_chunks (no attention)."""
+        for _ in range(n_chunks):
+            for l in range(N_LAYERS):
+                self.cache_k[l][:, self.tot:self.tot + CT].normal_()
+                self.cache_v[l][:, self.tot:self.tot + CT].normal_()
+            self.bank_update()
+
+    def bank_update(self):
+        c = self.chunk
+        pose = self.poses[c]
+        src_k = [ck[0, self.tot:self.tot + CT] for ck in self.cache_k]
+        src_v = [cv[0, self.tot:self.tot + CT] for cv in self.cache_v]
+        R = self.bank.add_chunk_from(src_k, src_v, pose, pose)
+        self.tot = self.bank.write_into_caches(self.cache_k, self.cache_v, R)
+        self.launches += 3        # pack copy, bank decision, gather
+        self.chunk += 1
+
+    def forward(self, time_attn=False):
+        from reworld_b200 import chunk_attention, rope_kv_store
+        from reworld_b200.ulysses import head_to_seq, seq_to_head
+        start_frame = (self.chunk * CT) // (TOK_H * TOK_W)
+        rope = self.RopeArgs(self.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
+        for l in range(N_LAYERS):
+            q, k, v = self.q[l], self.k[l], self.v[l]
+            if self.world > 1:
+                q, k, v = seq_to_head(q, self.group), seq_to_head(k, self.group), seq_to_head(v, self.group)
+                self.launches += 3
+            rope_kv_store(k, v, self.cache_k[l], self.cache_v[l], self.tot, rope=rope)
+            lk = self.tot + CT
+            if time_attn:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            o = chunk_attention(q, self.cache_k[l][:, :lk], self.cache_v[l][:, :lk], rope=rope, out=self.out[l])
+            if time_attn:
+                e1.record()
+                self.attn_events.append((e0, e1, lk))
+            if self.world > 1:
+                o = head_to_seq(o, HEADS, self.group)
+                self.launches += 1
+            self.launches += 2
+
+    def step(self, time_attn=False):
+        for _ in range(FORWARDS_PER_CHUNK):
+            self.forward(time_attn)
+        self.bank_update()
+
+
+def run_gpu(args):
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+    from reworld_b200 import _native
+    heads = HEADS // world
+    seq_shard = CT // world
+    ro = Rollout(dev, heads, seq_shard, world, rank, group)
+    ro.fill_bank(BUDGET + BANK_K + 2)          # steady state: bank full, 12-chunk cache
+    for _ in range(args.warmup):
+        ro.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches0 = ro.launches
+    ro.attn_events.clear()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            ro.step(time_attn=True)
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = (ro.launches - launches0) // args.steps
+    attn_ms = [a.elapsed_time(b) for a, b, _ in ro.attn_events]
+    attn_lk = [lk for _, _, lk in ro.attn_events]
+    _native.check_status(dev)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # e2e: host buffers through the public API, copies inside the timed region
+    e2e = run_e2e(ro, args, dev) if world == 1 else None
+
+    step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
+    attn_avg_ms = sum(attn_ms) / len(attn_ms)
+    per_launch_flops = attn_flops(CT, statistics.mean(attn_lk), heads)
+    burst, sustained, hbm, peak_src = load_peaks()
+    achieved = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12
+    traffic = profiled_traffic()
+    extra = {}
+    if rank == 0 and world == 1:
+        extra = gpu_side_baselines(ro, dev)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(step_flops / (ms_max * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, random-walk camera poses)",
+            "config": {"workload": WORKLOAD, "step": "one chunk: 5 forwards x 30 layers + bank update + gather",
+                       "Lq": CT, "Lk": LK, "layers": N_LAYERS, "heads": HEADS, "head_dim": HEAD_DIM,
+                       "parallelism": f"ulysses{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (12.5 GB of caches + 1.5 GB activations per step)"},
+            "ms_per_forward": round(ms_max / FORWARDS_PER_CHUNK, 3),
+            "chunks_per_s": round(1000.0 / ms_max, 3),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
+                         "peak_kind": f"bf16 sustained ({peak_src}); burst {burst}",
+                         "frac_of_burst": round(achieved / burst, 4),
+                         "kernel": "rw_attn_fwd", "avg_launch_ms": round(attn_avg_ms, 4),
+                         "flops_per_launch": per_launch_flops, "traffic": traffic},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        line.update(extra)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(ro, args, dev):
+    """Same chunk step through the public API with q/k/v of every forward coming
+    from pinned host memory and every layer's output copied back to pinned host
+    memory; copies run on side streams overlapped with the compute stream."""
+    from reworld_b200 import chunk_attention, rope_kv_store
+    comp = torch.cuda.current_stream(dev)
+    h2d = torch.cuda.Stream(dev)
+    d2h = torch.cuda.Stream(dev)
+    shape = (1, CT, HEADS, HEAD_DIM)
+    host_in = [torch.randn(3, *shape).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    host_out = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dev_in = [torch.empty((3, *shape), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dev_out = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_read = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_used + ev_read:
+        e.record(comp)
+    bytes_in = 3 * CT * HEADS * HEAD_DIM * 2
+    bytes_out = CT * HEADS * HEAD_DIM * 2
+
+    def step():
+        n = 0
+        for _f in range(FORWARDS_PER_CHUNK):
+            start_frame = (ro.chunk * CT) // (TOK_H * TOK_W)
+            rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
+            for l in range(N_LAYERS):
+                b = n & 1
+                with torch.cuda.stream(h2d):
+                    h2d.wait_event(ev_used[b])
+                    dev_in[b].copy_(host_in[b], non_blocking=True)
+                    ev_in[b].record(h2d)
+                comp.wait_event(ev_in[b])
+                comp.wait_event(ev_read[b])
+                q, k, v = dev_in[b][0], dev_in[b][1], dev_in[b][2]
+                rope_kv_store(k, v, ro.cache_k[l], ro.cache_v[l], ro.tot, rope=rope)
+                lk = ro.tot + CT
+                chunk_attention(q, ro.cache_k[l][:, :lk], ro.cache_v[l][:, :lk], rope=rope, out=dev_out[b])
+                ev_used[b].record(comp)
+                ev_out[b].record(comp)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_out[b])
+                    host_out[b].copy_(dev_out[b], non_blocking=True)
+                    ev_read[b].record(d2h)
+                n += 1
+        ro.bank_update()
+
+    for _ in range(max(1, args.warmup // 2)):
+        step()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(comp)
+    for _ in range(args.steps):
+        step()
+    comp.wait_stream(d2h)
+    t1.record(comp)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
+    n_io = FORWARDS_PER_CHUNK * N_LAYERS
+    return {"value": round(step_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 3),
+            "h2d_bytes_per_step": n_io * bytes_in, "d2h_bytes_per_step": n_io * bytes_out,
+            "path": "reworld_b200.rope_kv_store + chunk_attention with pinned host q/k/v in, output out, "
+                    "copies on side streams overlapped with compute"}
+
+
+def gpu_side_baselines(ro, dev):
+    """Library attention on the same single-layer shape, for context: flash-attn 2
+    (what the reference's attention() dispatches to on a GPU with the wheel
+    installed) and torch SDPA (cuDNN on this box); plus this kernel at the
+    literal 31680-key budget and the landmark gather bandwidth."""
+    from reworld_b200 import chunk_attention
+    out = {}
+    l = 0
+    q = ro.q[l]
+    k = ro.cache_k[l][:, :LK].contiguous()
+    v = ro.cache_v[l][:, :LK].contiguous()
+    fl = attn_flops(CT, LK, HEADS)
+
+    def timeit(fn, n=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    ms = timeit(lambda: chunk_attention(q, k, v))
+    out["attn_layer_ms"] = round(ms, 4)
+    out["attn_layer_tflops"] = round(fl / ms / 1e9, 1)
+    lk2 = BUDGET * CT
+    ms2 = timeit(lambda: chunk_attention(q, k[:, :lk2], v[:, :lk2]))
+    out["attn_layer_tflops_lk31680"] = round(attn_flops(CT, lk2, HEADS) / ms2 / 1e9, 1)
+    try:
+        import flash_attn
+        ms3 = timeit(lambda: flash_attn.flash_attn_func(q, k, v))
+        out["flash_attn2_layer_tflops"] = round(fl / ms3 / 1e9, 1)
+    except Exception as ex:   # noqa: BLE001
+        out["flash_attn2_layer_tflops"] = f"unavailable: {type(ex).__name__}"
+    try:
+        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        ms4 = timeit(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt))
+        out["torch_sdpa_layer_tflops"] = round(fl / ms4 / 1e9, 1)
+    except Exception as ex:   # noqa: BLE001
+        out["torch_sdpa_layer_tflops"] = f"unavailable: {type(ex).__name__}"
+    # gather bandwidth: the all-layer write_into_caches of the step
+    R = list(range(min(N_LANDMARK, len(ro.bank.bank))))
+    msg = timeit(lambda: ro.bank.write_into_caches(ro.cache_k, ro.cache_v, R), n=5)
+    nbytes = 2 * 2 * N_LAYERS * (N_SINK + RECENT_W + len(R)) * CT * ro.H * HEAD_DIM * 2   # read + write, k + v
+    out["gather_ms"] = round(msg, 3)
+    out["gather_gbs"] = round(nbytes / (msg * 1e-3) / 1e9, 1)
+    return out
+
+
+# ------------------------------------------------------------------ CPU baseline / reference arm
+def cpu_sample(heads, lq=CT, lk=LK, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, lq, heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, lk, heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, lk, heads, HEAD_DIM, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+def cpu_baseline(budget_s=15.0):
+    """The reference's CPU attention path (oracle port of wan_5b/modules/attention.py:
+    164-179, torch SDPA in bf16) on this host's cores, on a bounded sample of
+    the workload: h heads of one layer at Lq 2640 x Lk 34320."""
+    from oracle.attention import reference_attention_cpu
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    q, k, v = cpu_sample(1)
+    t = time.perf_counter()
+    reference_attention_cpu(q, k, v)
+    one = time.perf_counter() - t
+    heads = max(1, min(HEADS, int(budget_s / 3 / max(one, 1e-3))))
+    q, k, v = cpu_sample(heads)
+    reps = 2
+    t = time.perf_counter()
+    for _ in range(reps):
+        reference_attention_cpu(q, k, v)
+    dt = (time.perf_counter() - t) / reps
+    fl = attn_flops(CT, LK, heads)
+    return {"value": round(fl / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{heads} of 24 heads of one layer, Lq {CT} x Lk {LK}, bf16 torch SDPA on CPU, "
+                      f"{reps} repeats after 1 warm-up ({dt:.2f} s per repeat)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.attention import reference_attention_cpu
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    q, k, v = cpu_sample(1)
+    t = time.perf_counter()
+    reference_attention_cpu(q, k, v)
+    one = time.perf_counter() - t
+    # each step: as many heads of one layer as fit in ~budget/(steps+warmup) seconds
+    per_step = max(0.5, args.cpu_seconds * 3 / max(1, args.steps + args.warmup))
+    heads = max(1, min(HEADS, int(per_step / max(one, 1e-3))))
+    q, k, v = cpu_sample(heads)
+    for _ in range(args.warmup):
+        reference_attention_cpu(q, k, v)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        reference_attention_cpu(q, k, v)
+    dt = (time.perf_counter() - t) / args.steps
+    fl = attn_flops(CT, LK, heads)
+    val = round(fl / dt / 1e12, 4)
+    sample = (f"{heads} of 24 heads of one layer per step, Lq {CT} x Lk {LK}, bf16 torch SDPA on CPU "
+              f"(the reference attention() branch without flash-attention)")
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": WORKLOAD, "Lq": CT, "Lk": LK, "layers": N_LAYERS, "heads": HEADS,
+                       "head_dim": HEAD_DIM, "parallelism": "cpu"},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()
