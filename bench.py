@@ -232,11 +232,13 @@ def run_gpu(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed_steps")
         e0.record()
         for _ in range(args.steps):
             ro.step(time_attn=True)
         e1.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     ms = e0.elapsed_time(e1) / args.steps
@@ -425,25 +427,24 @@ def cpu_sample(heads, lq=CT, lk=LK, seed=0):
 def cpu_baseline(budget_s=15.0):
     """The reference's CPU attention path (oracle port of wan_5b/modules/attention.py:
     164-179, torch SDPA in bf16) on this host's cores, on a bounded sample of
-    the workload: h heads of one layer at Lq 2640 x Lk 34320."""
+    the workload: whole layers (24 heads, Lq 2640 x Lk 34320) repeated for about
+    budget_s seconds."""
     from oracle.attention import reference_attention_cpu
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    q, k, v = cpu_sample(1)
+    q, k, v = cpu_sample(HEADS)
     t = time.perf_counter()
-    reference_attention_cpu(q, k, v)
+    reference_attention_cpu(q, k, v)                 # warm-up, also sizes the sample
     one = time.perf_counter() - t
-    heads = max(1, min(HEADS, int(budget_s / 3 / max(one, 1e-3))))
-    q, k, v = cpu_sample(heads)
-    reps = 2
+    reps = max(1, int(budget_s / max(one, 1e-3)))
     t = time.perf_counter()
     for _ in range(reps):
         reference_attention_cpu(q, k, v)
     dt = (time.perf_counter() - t) / reps
-    fl = attn_flops(CT, LK, heads)
+    fl = attn_flops(CT, LK, HEADS)
     return {"value": round(fl / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-            "sample": f"{heads} of 24 heads of one layer, Lq {CT} x Lk {LK}, bf16 torch SDPA on CPU, "
-                      f"{reps} repeats after 1 warm-up ({dt:.2f} s per repeat)"}
+            "sample": f"{reps} layers (24 heads, Lq {CT} x Lk {LK}) of bf16 torch SDPA on CPU after 1 warm-up, "
+                      f"{dt:.3f} s per layer ({reps * dt:.1f} s total)"}
 
 
 def run_reference(args):
@@ -454,24 +455,25 @@ def run_reference(args):
     from oracle.attention import reference_attention_cpu
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    q, k, v = cpu_sample(1)
+    q, k, v = cpu_sample(HEADS)
     t = time.perf_counter()
     reference_attention_cpu(q, k, v)
     one = time.perf_counter() - t
-    # each step: as many heads of one layer as fit in ~budget/(steps+warmup) seconds
-    per_step = max(0.5, args.cpu_seconds * 3 / max(1, args.steps + args.warmup))
-    heads = max(1, min(HEADS, int(per_step / max(one, 1e-3))))
-    q, k, v = cpu_sample(heads)
+    # each step: whole layers of the chunk, as many as fit in the CPU budget spread over the run
+    per_step = max(one, args.cpu_seconds / max(1, args.steps + args.warmup))
+    layers = max(1, min(N_LAYERS * FORWARDS_PER_CHUNK, int(per_step / max(one, 1e-3))))
     for _ in range(args.warmup):
-        reference_attention_cpu(q, k, v)
+        for _l in range(layers):
+            reference_attention_cpu(q, k, v)
     t = time.perf_counter()
     for _ in range(args.steps):
-        reference_attention_cpu(q, k, v)
+        for _l in range(layers):
+            reference_attention_cpu(q, k, v)
     dt = (time.perf_counter() - t) / args.steps
-    fl = attn_flops(CT, LK, heads)
+    fl = layers * attn_flops(CT, LK, HEADS)
     val = round(fl / dt / 1e12, 4)
-    sample = (f"{heads} of 24 heads of one layer per step, Lq {CT} x Lk {LK}, bf16 torch SDPA on CPU "
-              f"(the reference attention() branch without flash-attention)")
+    sample = (f"{layers} layers (24 heads, Lq {CT} x Lk {LK}) per step of bf16 torch SDPA on CPU "
+              f"(the reference attention() branch without flash-attention), {dt:.2f} s per step")
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
