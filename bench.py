@@ -114,7 +114,7 @@ def load_peaks():
 
 def profiled_traffic():
     """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "attn_fwd_ncu.md")
+    p = os.path.join(ROOT, "profiles", "attn_fwd_ncu.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):
