@@ -38,6 +38,7 @@ constexpr int BM = 128;                     // query rows per tile
 constexpr int BN = 128;                     // keys per tile
 constexpr int HD = 128;                     // head dim
 constexpr int NSLOT = 5;                    // K/V ring slots (K_j and V_j alternate)
+constexpr int NSTEPBAR = 3;                 // step_free barriers (>= 3 keeps producer waits unambiguous)
 constexpr int TILE_BYTES = BM * HD * 2;     // 32 KB: every Q/K/V/O tile
 constexpr int HALF_BYTES = TILE_BYTES / 2;  // 128 rows x 64 columns (one TMA box)
 constexpr int NUM_THREADS = 384;
@@ -58,7 +59,6 @@ struct Params {
 
 struct __align__(8) Barriers {
   uint64_t slot_full[NSLOT];
-  uint64_t slot_empty[NSLOT];
   uint64_t q_full[2];
   uint64_t q_ready[2];
   uint64_t s_full[2];
@@ -66,6 +66,7 @@ struct __align__(8) Barriers {
   uint64_t o_done[2];
   uint64_t epi[2];
   uint64_t drain;
+  uint64_t step_free[NSTEPBAR];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -110,10 +111,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int kv_tail = p.Lk - (n_kv - 1) * BN;  // valid keys in the last tile, 1..128
 
   if (threadIdx.x == WARP_LOAD * 32) {
-    for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(&sb.slot_full[s], 1);
-      mbar_init(&sb.slot_empty[s], 1);
-    }
+    for (int s = 0; s < NSLOT; ++s) mbar_init(&sb.slot_full[s], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sb.q_full[i], 1);
       mbar_init(&sb.q_ready[i], BM);
@@ -123,6 +121,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&sb.epi[i], BM);
     }
     mbar_init(&sb.drain, 1);
+    for (int t = 0; t < NSTEPBAR; ++t) mbar_init(&sb.step_free[t], 1);
     sb.abort_flag = 0;
     fence_mbar_init();
   }
@@ -134,9 +133,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
+  // Registers: the launch gives 168 per thread (384 x 168 = 64512); the producer /
+  // MMA warpgroup (warps 8-11) keeps 72 and hands the rest to the two softmax
+  // warpgroups (216): 128 x 72 + 256 x 216 = 64512.  Each role adjusts in its own branch.
 
   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer
+    setmaxnreg_dec_72();
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -155,10 +158,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int j = 0; j < n_kv && ok; ++j) {
         for (int t = 0; t < 2; ++t) {
-          const uint32_t s = g % NSLOT, use = g / NSLOT;
-          if (!mbar_wait(&sb.slot_empty[s], (use & 1) ^ 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_LOAD)) {
-            ok = false;
-            break;
+          const uint32_t s = g % NSLOT;
+          if (g >= (uint32_t)NSLOT) {
+            // use g refills the slot of use u = g - NSLOT, freed by key tile (u + 1) / 2
+            const uint32_t step = (g - NSLOT + 1) / 2;
+            if (!mbar_wait(&sb.step_free[step % NSTEPBAR], (step / NSTEPBAR) & 1, &sb.abort_flag, p.status,
+                           RW_STATUS_TIMEOUT_LOAD)) {
+              ok = false;
+              break;
+            }
           }
           uint8_t* dst = smem_ring + s * TILE_BYTES;
           const CUtensorMap* m = t == 0 ? &tm_k : &tm_v;
@@ -177,6 +185,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
+    // A single thread issues both query tiles' MMAs in the strict alternation
+    // PV0(j-1), QK0(j), PV1(j-1), QK1(j): each softmax warpgroup then has the
+    // other tile's two GEMMs of time to turn its S tile into P.  Per key tile it
+    // commits three times: S0 ready, S1 ready, and step_free (K_j and V_{j-1}
+    // no longer read), which the producer waits on before refilling those slots.
+    setmaxnreg_dec_72();
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
       constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, HD, 0, 1);  // P from TMEM, V MN-major
@@ -190,28 +204,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-          const uint64_t da = umma_desc(q_addr[i] + off, 16, 1024);
-          const uint64_t db = umma_desc(k_addr + off, 16, 1024);
-          mma_ss(tmem + tcol_s(i), da, db, IDESC_QK, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + tcol_s(i), umma_desc(q_addr[i] + off, 16, 1024), umma_desc(k_addr + off, 16, 1024),
+                 IDESC_QK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int i, uint32_t v_addr, bool acc) {
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t db = umma_desc(v_addr + kk * 2048, HALF_BYTES, 1024);
-          mma_ts(tmem + tcol_o(i), tmem + tcol_s(i) + kk * 8, db, IDESC_PV, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts(tmem + tcol_o(i), tmem + tcol_s(i) + kk * 8, umma_desc(v_addr + kk * 2048, HALF_BYTES, 1024),
+                 IDESC_PV, (acc || kk > 0) ? 1u : 0u);
       };
 
-      uint32_t g = 0;
+      // ring position of K_j (use 2j) and V_j (use 2j+1), advanced incrementally
+      uint32_t sK = 0, parK = 0, sV = 1, parV = 0;
       uint32_t v_prev_slot = 0, v_prev_par = 0;
+      uint32_t fs = 0, fpar = 0;  // step_free barrier of key tile j
       for (int j = 0; j < n_kv && ok; ++j) {
-        const uint32_t sK = g % NSLOT, parK = (g / NSLOT) & 1;
-        ++g;
-        const uint32_t sV = g % NSLOT, parV = (g / NSLOT) & 1;
-        ++g;
-        if (!(ok = mbar_wait(&sb.slot_full[sK], parK, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
-        const uint32_t k_addr = ring_addr + sK * TILE_BYTES;
         const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
         if (j > 0) {
           if (!(ok = mbar_wait(&sb.p_ready[0], (j - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
@@ -221,6 +229,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           issue_pv(0, vp_addr, j > 1);
         }
+        if (!(ok = mbar_wait(&sb.slot_full[sK], parK, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
+        const uint32_t k_addr = ring_addr + sK * TILE_BYTES;
         issue_qk(0, k_addr);
         tc_commit(&sb.s_full[0]);
         if (has_q1) {
@@ -233,10 +243,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           issue_qk(1, k_addr);
           tc_commit(&sb.s_full[1]);
         }
-        if (j > 0) tc_commit(&sb.slot_empty[v_prev_slot]);
-        tc_commit(&sb.slot_empty[sK]);
+        tc_commit(&sb.step_free[fs]);  // K_j and V_{j-1} released once everything above completes
+        if (++fs == NSTEPBAR) { fs = 0; fpar ^= 1; }
         v_prev_slot = sV;
         v_prev_par = parV;
+        sK += 2;
+        if (sK >= NSLOT) { sK -= NSLOT; parK ^= 1; }
+        sV += 2;
+        if (sV >= NSLOT) { sV -= NSLOT; parV ^= 1; }
       }
       if (ok) {
         const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
@@ -254,7 +268,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               tc_commit(&sb.o_done[1]);
             }
           }
-          tc_commit(&sb.slot_empty[v_prev_slot]);
         }
       }
       // All MMAs issued by this thread complete before teardown.
@@ -264,6 +277,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax + epilogue
+    setmaxnreg_inc_216();
     const int i = warp >> 2;  // query tile of this warpgroup
     const int r = threadIdx.x & 127;
     const bool active = (i == 0) || has_q1;
@@ -280,7 +294,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&sb.q_ready[i]);
       }
       float m_used = -INFINITY;
-      float l_part[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t l2 = 0ull;  // packed (even-column, odd-column) partial row sums
+      float l_lo = 0.f, l_hi = 0.f;
       for (int j = 0; j < n_kv && ok; ++j) {
         if (!(ok = warp_wait(&sb.s_full[i], j & 1, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX))) break;
         tc_fence_after();
@@ -297,26 +312,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int e = 0; e < 32; ++e)
               if (32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
         }
-        float mx[8];
+        // row maximum: 3-input max tree
+        float mx[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(sr[q >> 1][(q & 1) * 16]);
+        for (int c = 0; c < 4; ++c) {
+          float a = fmax3(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]), __uint_as_float(sr[c][2]));
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = (c * 2) + (e >> 4);
-            mx[q] = fmaxf(mx[q], __uint_as_float(sr[c][e]));
-          }
-        const float row_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          for (int e = 3; e + 1 < 32; e += 2)
+            a = fmax3(a, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+          mx[c] = fmaxf(a, __uint_as_float(sr[c][31]));
+        }
+        const float row_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         const float m_new = fmaxf(m_used, row_max);
         const bool need = (m_new - m_used) * sl2 > RESCALE_THRESHOLD;
         float alpha = 1.f;
         if (need) {
           alpha = fast_exp2((m_used - m_new) * sl2);
           m_used = m_new;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) l_part[q] *= alpha;
+          l2 = f2_pack(l_lo * alpha, l_hi * alpha);
+          f2_unpack(l2, l_lo, l_hi);
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // O_i is quiescent here: PV_i(j-1) completed before S_i(j) was published.
@@ -331,22 +345,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + 32 * c, o);
           }
         }
+        // P = 2^(s*scale_log2 - m*scale_log2): 5 of 8 column pairs on MUFU (ex2),
+        // 3 of 8 on the FMA pipe (exp2_poly_pair), so neither pipe limits the
+        // tile; the exponent arguments and the row sum use packed fp32x2 math.
         const float nm = -m_used * sl2;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t pk[32];
+          uint64_t lacc[2] = {0ull, 0ull};
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int col = 64 * h + 2 * e;
-            const float s0 = __uint_as_float(sr[col >> 5][col & 31]);
-            const float s1 = __uint_as_float(sr[(col + 1) >> 5][(col + 1) & 31]);
-            const float p0 = fast_exp2(fmaf(s0, sl2, nm));
-            const float p1 = fast_exp2(fmaf(s1, sl2, nm));
-            l_part[e & 3] += p0 + p1;
+            const uint64_t sv = f2_pack(__uint_as_float(sr[col >> 5][col & 31]),
+                                        __uint_as_float(sr[(col + 1) >> 5][(col + 1) & 31]));
+            const uint64_t xv = ffma2(sv, sl2x2, nmx2);
+            float x0, x1, p0, p1;
+            f2_unpack(xv, x0, x1);
+            if ((e & 7) >= 5) {
+              exp2_poly_pair(x0, x1, p0, p1);
+            } else {
+              p0 = fast_exp2(x0);
+              p1 = fast_exp2(x1);
+            }
+            lacc[e & 1] = fadd2(lacc[e & 1], f2_pack(p0, p1));
             pk[e] = pack_bf16x2(p0, p1);
           }
+          l2 = fadd2(l2, fadd2(lacc[0], lacc[1]));
           tmem_st32(tS + 32 * h, pk);
         }
+        f2_unpack(l2, l_lo, l_hi);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sb.p_ready[i]);
@@ -355,7 +383,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (ok) ok = warp_wait(&sb.o_done[i], 0, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX);
       if (ok) {
         tc_fence_after();
-        const float l = (l_part[0] + l_part[1]) + (l_part[2] + l_part[3]);
+        const float l = l_lo + l_hi;
         const float inv = l > 0.f ? 1.f / l : 0.f;
         uint8_t* out = smem_q[i];
 #pragma unroll 1
@@ -388,6 +416,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+  } else {
+    setmaxnreg_dec_72();  // idle warps 10-11
   }
 
   tc_fence_before();
