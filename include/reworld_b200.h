@@ -58,6 +58,10 @@ typedef struct rw_rope {
 
 /* Chunk attention forward: o = softmax(q k^T * softmax_scale) v per (batch, head),
  * non-causal, bf16 in/out, fp32 accumulation (tcgen05/TMEM, TMA-fed).
+ * workspace (device memory, 16-byte aligned, rw_attn_workspace_bytes() bytes)
+ * lets the last partial wave of work be split along the keys and merged by a
+ * second kernel; with workspace == NULL (or too small) every (head, query-tile
+ * pair) runs whole in one CTA — same results, fewer CTAs in the last wave.
  * Replaces wan_5b/modules/attention.py:133-179 `attention(q, k, v)` (and the
  * flash_attn_varlen_func call at :111-127) as called from
  * wan_5b/modules/action_model.py:302 with k/v = kv_cache[:, :local_end].
@@ -69,7 +73,12 @@ typedef struct rw_rope {
 int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, int D,
                 long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh,
                 long long v_sb, long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh,
-                float softmax_scale, const rw_rope_t* rope, int* status, void* stream);
+                float softmax_scale, const rw_rope_t* rope, void* workspace, long long workspace_bytes,
+                int* status, void* stream);
+
+/* Workspace bytes rw_attn_fwd uses for this shape on the current device (0 when
+ * the work fills whole waves). */
+long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H);
 
 /* RoPE(+PM-RoPE) on the new chunk's K and the cache write of K and V:
  * cache_k[b, dst_start + t] = rope(k[b, t]), cache_v[b, dst_start + t] = v[b, t]

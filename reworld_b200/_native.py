@@ -47,7 +47,8 @@ class RwCopyDesc(ctypes.Structure):
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "rw_attn_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int] + [c_ll] * 12
-                    + [c_float, ctypes.POINTER(RwRope), c_vp, c_vp]),
+                    + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
+    "rw_attn_workspace_bytes": (c_ll, [c_int, c_int, c_int, c_int]),
     "rw_rope_kv_store": (c_int, [c_vp] * 6 + [c_int] * 5 + [c_ll] * 18 + [ctypes.POINTER(RwRope), c_vp]),
     "rw_copy_chunks": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "rw_bank_step": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp]),
@@ -57,7 +58,7 @@ _SIGNATURES = {
     "rw_abi_version": (c_int, []),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 _lib = None
 
 
@@ -74,7 +75,7 @@ def lib():
     path = lib_path()
     if not os.path.exists(path):
         raise ImportError(
-            f"reworld_b200 CUDA library not built ({path} missing); run `python -m reworld_b200.build`")
+            f"reworld_b200 CUDA library not built ({path} missing); run `python reworld_b200/build.py`")
     handle = ctypes.CDLL(path)
     for name, (res, args) in _SIGNATURES.items():
         fn = getattr(handle, name, None)

@@ -26,6 +26,21 @@ def _prep(t):
     return t
 
 
+_workspaces = {}
+
+
+def _workspace(device, nbytes):
+    """Per-device scratch for the key-split tail of the attention kernel (grown on demand)."""
+    if nbytes <= 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = ws
+    return ws
+
+
 def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None):
     """softmax(q k^T * scale) v over every key (no mask), bf16, fp32 accumulation.
 
@@ -51,6 +66,7 @@ def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None):
     lib = _native.lib()
     with torch.cuda.device(q.device):
         st = _native.status_tensor(q.device)
+        ws = _workspace(q.device, lib.rw_attn_workspace_bytes(B, Lq, Lk, H))
         code = lib.rw_attn_fwd(
             c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()), c_vp(out.data_ptr()),
             B, Lq, Lk, H, D,
@@ -59,6 +75,7 @@ def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None):
             v.stride(0), v.stride(1), v.stride(2),
             out.stride(0), out.stride(1), out.stride(2),
             scale, ctypes.byref(rope_struct) if rope_struct is not None else None,
+            c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
             c_vp(st.data_ptr()), _native.stream_ptr(q.device))
     _native.check(code, "rw_attn_fwd")
     return out

@@ -2,8 +2,8 @@
 
 Each .cu file under csrc/ is compiled with nvcc for `-gencode
 arch=compute_100a,code=sm_100a` and the objects are linked into one shared
-library that the package loads with ctypes.  Run `python -m reworld_b200.build`
-or call build().
+library that the package loads with ctypes.  Run `python reworld_b200/build.py`
+(by path: importing the package requires the library to exist) or call build().
 """
 import concurrent.futures
 import os

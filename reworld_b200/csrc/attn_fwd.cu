@@ -49,13 +49,25 @@ constexpr int WARP_LOAD = 8;
 constexpr int WARP_MMA = 9;
 constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
 
+// Work split.  A unit is one (batch, head, query-tile pair) over all keys.  The
+// first n_whole units run whole (one CTA each, result written directly); the
+// remaining n_tail units are cut into `splits` key ranges each, ordered
+// piece-major so that concurrently running CTAs share a head and a key range
+// (K/V tiles then come from L2), and write unnormalised partial results to the
+// workspace, merged by combine_kernel.  splits == 1 means no tail.
 struct Params {
   int B, Lq, Lk, H;
+  int nqp;              // query-tile pairs per (batch, head)
+  int n_whole, n_tail, splits;
   float scale_log2;
   int rope_on;
   rw_rope_t rope;
   int* status;
+  float* scratch;       // n_tail * splits partial slots (column-major O, then m, then l)
 };
+
+// one partial slot: O [128 columns][256 rows] fp32, m [256], l [256]
+constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
 
 struct __align__(8) Barriers {
   uint64_t slot_full[NSLOT];
@@ -103,12 +115,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int bidx = blockIdx.z;
-  const int q_row0 = blockIdx.x * (2 * BM);
+  const int n_kv_all = (p.Lk + BN - 1) / BN;
+  const int kv_tail = p.Lk - (n_kv_all - 1) * BN;  // valid keys in the last key tile, 1..128
+  int unit, kv0, kv1, slot = -1;
+  if ((int)blockIdx.x < p.n_whole) {
+    unit = blockIdx.x;
+    kv0 = 0;
+    kv1 = n_kv_all;
+  } else {
+    const int t = blockIdx.x - p.n_whole;
+    const int e = t % p.n_tail, piece = t / p.n_tail;
+    unit = p.n_whole + e;
+    kv0 = (int)((long long)piece * n_kv_all / p.splits);
+    kv1 = (int)((long long)(piece + 1) * n_kv_all / p.splits);
+    slot = e * p.splits + piece;
+  }
+  const int qp = unit % p.nqp;
+  const int head = (unit / p.nqp) % p.H;
+  const int bidx = unit / (p.nqp * p.H);
+  const int q_row0 = qp * (2 * BM);
   const bool has_q1 = (q_row0 + BM) < p.Lq;
-  const int n_kv = (p.Lk + BN - 1) / BN;
-  const int kv_tail = p.Lk - (n_kv - 1) * BN;  // valid keys in the last tile, 1..128
+  const int n_kv = kv1 - kv0;  // key tiles of this CTA
 
   if (threadIdx.x == WARP_LOAD * 32) {
     for (int s = 0; s < NSLOT; ++s) mbar_init(&sb.slot_full[s], 1);
@@ -171,8 +198,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* dst = smem_ring + s * TILE_BYTES;
           const CUtensorMap* m = t == 0 ? &tm_k : &tm_v;
           mbar_expect_tx(&sb.slot_full[s], TILE_BYTES);
-          tma_load_4d_hint(dst, m, &sb.slot_full[s], 0, head, j * BN, bidx, pol);
-          tma_load_4d_hint(dst + HALF_BYTES, m, &sb.slot_full[s], 64, head, j * BN, bidx, pol);
+          tma_load_4d_hint(dst, m, &sb.slot_full[s], 0, head, (kv0 + j) * BN, bidx, pol);
+          tma_load_4d_hint(dst + HALF_BYTES, m, &sb.slot_full[s], 64, head, (kv0 + j) * BN, bidx, pol);
           ++g;
         }
       }
@@ -305,7 +332,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) reg_fence32(sr[c]);
-        if (j == n_kv - 1 && kv_tail < BN) {
+        if (kv0 + j == n_kv_all - 1 && kv_tail < BN) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -379,9 +406,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_before();
         mbar_arrive(&sb.p_ready[i]);
       }
-      // ---- epilogue: O_i / l -> bf16 -> smem (reusing Q_i) -> TMA store
+      // ---- epilogue
       if (ok) ok = warp_wait(&sb.o_done[i], 0, sb, p.status, RW_STATUS_TIMEOUT_SOFTMAX);
-      if (ok) {
+      if (ok && slot >= 0) {
+        // partial key range: unnormalised O (column-major, coalesced across the
+        // warp's rows), the exponent base m and the row sum l, for combine_kernel
+        tc_fence_after();
+        float* base = p.scratch + (size_t)slot * SLOT_FLOATS;
+        const int row = i * BM + r;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) base[(size_t)(32 * c + e) * 256 + row] = __uint_as_float(o[e]);
+        }
+        base[128 * 256 + row] = m_used;
+        base[128 * 256 + 256 + row] = l_lo + l_hi;
+      } else if (ok) {
+        // whole unit: O_i / l -> bf16 -> smem (reusing Q_i) -> TMA store
         tc_fence_after();
         const float l = l_lo + l_hi;
         const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -428,16 +473,99 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Merges the partial key ranges of each split unit: m = max m_p,
+// o = sum_p 2^((m_p - m) * scale_log2) * O_p / sum_p 2^((m_p - m) * scale_log2) * l_p.
+// One thread per query row; partial O is column-major so loads coalesce.
+__global__ void __launch_bounds__(128)
+    combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
+                   long long o_sh, int Lq, int H, int nqp, int n_whole, int splits, float scale_log2) {
+  const int e = blockIdx.x, i = blockIdx.y, r = threadIdx.x;
+  const int unit = n_whole + e;
+  const int qp = unit % nqp, head = (unit / nqp) % H, b = unit / (nqp * H);
+  const int row_tok = qp * 2 * BM + i * BM + r;
+  if (row_tok >= Lq) return;
+  const int row = i * BM + r;
+  const float* slot0 = scratch + (size_t)e * splits * SLOT_FLOATS;
+  float m = -INFINITY;
+  for (int pc = 0; pc < splits; ++pc) m = fmaxf(m, slot0[pc * SLOT_FLOATS + 128 * 256 + row]);
+  float acc[128];
+#pragma unroll
+  for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+  float L = 0.f;
+  for (int pc = 0; pc < splits; ++pc) {
+    const float* sp = slot0 + pc * SLOT_FLOATS;
+    const float w = exp2f((sp[128 * 256 + row] - m) * scale_log2);
+    L += w * sp[128 * 256 + 256 + row];
+#pragma unroll
+    for (int c = 0; c < 128; ++c) acc[c] += w * sp[(size_t)c * 256 + row];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  uint4* dst = reinterpret_cast<uint4*>(out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh));
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    uint4 v;
+    v.x = pack_bf16x2(acc[8 * q + 0] * inv, acc[8 * q + 1] * inv);
+    v.y = pack_bf16x2(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
+    v.z = pack_bf16x2(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
+    v.w = pack_bf16x2(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
+    dst[q] = v;
+  }
+}
+
+// Chooses how many units run whole and into how many key ranges the rest is
+// cut: minimises (whole waves) + (waves of pieces) / splits + a per-wave cost of
+// ~1 % of a unit for each wave of pieces (CTA start, Q load, pipeline ramp,
+// partial store); with no workspace, everything runs whole.
+struct Schedule {
+  int n_whole, n_tail, splits;
+};
+
+inline Schedule plan(int units, int n_kv, int sms, bool allow_split) {
+  Schedule best{units, 0, 1};
+  double best_cost = (double)((units + sms - 1) / sms);
+  if (!allow_split || sms <= 0) return best;
+  const int full_waves = units / sms;
+  for (int k = full_waves; k >= 0 && k >= full_waves - 1; --k) {
+    const int tail = units - k * sms;
+    if (tail <= 0) continue;
+    for (int S = 2; S <= 16 && S <= n_kv; ++S) {
+      const long long pieces = (long long)tail * S;
+      const long long waves = (pieces + sms - 1) / sms;
+      const double cost = k + (double)waves / S + 0.01 * (double)waves;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = Schedule{k * sms, tail, S};
+      }
+    }
+  }
+  return best;
+}
+
+inline int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms;
+}
+
 }  // namespace attn
 }  // namespace rw
 
 using namespace rw;
 
+extern "C" long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H) {
+  if (B < 1 || Lq < 1 || Lk < 1 || H < 1) return 0;
+  const int nqp = (Lq + 2 * attn::BM - 1) / (2 * attn::BM);
+  const int n_kv = (Lk + attn::BN - 1) / attn::BN;
+  const attn::Schedule sc = attn::plan(B * H * nqp, n_kv, attn::sm_count(), true);
+  return (long long)sc.n_tail * sc.splits * attn::SLOT_FLOATS * (long long)sizeof(float);
+}
+
 extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H,
                            int D, long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl,
                            long long k_sh, long long v_sb, long long v_sl, long long v_sh, long long o_sb,
-                           long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope, int* status,
-                           void* stream) {
+                           long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope,
+                           void* workspace, long long workspace_bytes, int* status, void* stream) {
   if (!q || !k || !v || !o) return RW_ERR_INVALID_ARG;
   if (D != attn::HD) return RW_ERR_UNSUPPORTED;
   if (B < 1 || Lq < 1 || Lk < 1 || H < 1 || B > 65535 || H > 65535) return RW_ERR_INVALID_ARG;
@@ -470,7 +598,26 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
     return RW_ERR_DRIVER;
   static unsigned long long attr_done = 0;
   if (!ensure_smem_attr((const void*)attn::attn_fwd_kernel, attn::SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
-  dim3 grid((Lq + 2 * attn::BM - 1) / (2 * attn::BM), H, B);
-  attn::attn_fwd_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(mq, mk, mv, mo, prm);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  prm.nqp = (Lq + 2 * attn::BM - 1) / (2 * attn::BM);
+  const int n_kv = (Lk + attn::BN - 1) / attn::BN;
+  const int units = B * H * prm.nqp;
+  attn::Schedule sc = attn::plan(units, n_kv, attn::sm_count(), workspace != nullptr);
+  const long long need = (long long)sc.n_tail * sc.splits * attn::SLOT_FLOATS * (long long)sizeof(float);
+  if (sc.splits > 1 && (workspace_bytes < need || !aligned16(workspace))) sc = attn::Schedule{units, 0, 1};
+  prm.n_whole = sc.n_whole;
+  prm.n_tail = sc.n_tail;
+  prm.splits = sc.splits;
+  prm.scratch = (float*)workspace;
+  const long long grid = (long long)sc.n_whole + (long long)sc.n_tail * sc.splits;
+  if (grid > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
+  attn::attn_fwd_kernel<<<(unsigned)grid, attn::NUM_THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(mq, mk, mv, mo,
+                                                                                                     prm);
+  if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
+  if (sc.splits > 1) {
+    attn::combine_kernel<<<dim3(sc.n_tail, 2), 128, 0, (cudaStream_t)stream>>>(
+        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, prm.nqp, sc.n_whole, sc.splits,
+        prm.scale_log2);
+    if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
+  }
+  return RW_OK;
 }

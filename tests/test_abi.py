@@ -42,17 +42,17 @@ def test_struct_sizes_match_header():
 
 def test_attn_rejects_bad_arguments_without_launching():
     lib = _native.lib()
-    args = [None] * 4 + [1, 128, 128, 1, 128] + [0] * 12 + [0.1, None, None, None]
+    args = [None] * 4 + [1, 128, 128, 1, 128] + [0] * 12 + [0.1, None, None, 0, None, None]
     assert lib.rw_attn_fwd(*args) == -1                    # null pointers
     p = ctypes.c_void_p(16)
     st = [128 * 128, 128, 128] * 4
-    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 64, *st, 0.1, None, None, None) == -2   # head_dim 64
-    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 0, 1, 128, *st, 0.1, None, None, None) == -1    # Lk = 0
-    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *st, -1.0, None, None, None) == -1  # scale <= 0
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 64, *st, 0.1, None, None, 0, None, None) == -2   # head_dim 64
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 0, 1, 128, *st, 0.1, None, None, 0, None, None) == -1    # Lk = 0
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *st, -1.0, None, None, 0, None, None) == -1  # scale <= 0
     odd = ctypes.c_void_p(18)
-    assert lib.rw_attn_fwd(odd, p, p, p, 1, 128, 128, 1, 128, *st, 0.1, None, None, None) == -1  # misaligned
+    assert lib.rw_attn_fwd(odd, p, p, p, 1, 128, 128, 1, 128, *st, 0.1, None, None, 0, None, None) == -1  # misaligned
     bad = [128 * 128, 130, 128] * 4
-    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *bad, 0.1, None, None, None) == -1  # stride % 8
+    assert lib.rw_attn_fwd(p, p, p, p, 1, 128, 128, 1, 128, *bad, 0.1, None, None, 0, None, None) == -1  # stride % 8
 
 
 def test_other_entry_points_reject_bad_arguments():
@@ -77,3 +77,11 @@ def test_import_fails_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "lib_path", lambda: str(tmp_path / "missing.so"))
     with pytest.raises(ImportError):
         _native.lib()
+
+
+def test_attn_workspace_plan():
+    lib = _native.lib()
+    # 704x1280 chunk over the 13-chunk cache: 264 query-pair units, a split tail
+    n = lib.rw_attn_workspace_bytes(1, 2640, 34320, 24)
+    assert n > 0 and n % (4 * (128 * 256 + 512)) == 0
+    assert lib.rw_attn_workspace_bytes(0, 1, 1, 1) == 0

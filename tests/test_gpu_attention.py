@@ -165,3 +165,30 @@ def test_attention_full_size_heads_vs_fp32_reference(cuda):
         err = (out[0, :, h].float() - ref).abs()
         assert err.max().item() < MAX_ABS and err.mean().item() < MEAN_ABS
     _status_clean()
+
+
+@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 660, 2640, 24), (2, 300, 1000, 2)])
+def test_attention_key_split_matches_unsplit(cuda, B, Lq, Lk, H):
+    """The key-split last wave (workspace given) and the whole-unit path (no
+    workspace) compute the same attention."""
+    import ctypes
+    from reworld_b200 import _native, chunk_attention
+    g = torch.Generator(device=cuda).manual_seed(Lq + Lk)
+    q = torch.randn(B, Lq, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    lib = _native.lib()
+    assert lib.rw_attn_workspace_bytes(B, Lq, Lk, H) > 0      # these shapes do split
+    split = chunk_attention(q, k, v)
+    whole = torch.empty_like(q)
+    st = _native.status_tensor(cuda)
+    code = lib.rw_attn_fwd(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+                           ctypes.c_void_p(v.data_ptr()), ctypes.c_void_p(whole.data_ptr()), B, Lq, Lk, H, 128,
+                           *q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *whole.stride()[:3],
+                           1.0 / math.sqrt(128), None, None, 0, ctypes.c_void_p(st.data_ptr()),
+                           _native.stream_ptr(cuda))
+    assert code == 0
+    torch.cuda.synchronize()
+    err = (split.float() - whole.float()).abs()
+    assert err.max().item() < 1e-2 and err.mean().item() < 1e-4
+    _status_clean()
