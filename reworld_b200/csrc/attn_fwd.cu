@@ -372,8 +372,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + 32 * c, o);
           }
         }
-        // P = 2^(s*scale_log2 - m*scale_log2): 5 of 8 column pairs on MUFU (ex2),
-        // 3 of 8 on the FMA pipe (exp2_poly_pair), so neither pipe limits the
+        // P = 2^(s*scale_log2 - m*scale_log2): every other column pair on MUFU (ex2),
+        // the rest on the FMA pipe (exp2_poly_pair), so neither pipe limits the
         // tile; the exponent arguments and the row sum use packed fp32x2 math.
         const float nm = -m_used * sl2;
         const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t xv = ffma2(sv, sl2x2, nmx2);
             float x0, x1, p0, p1;
             f2_unpack(xv, x0, x1);
-            if ((e & 7) >= 5) {
+            if ((e & 1) == 1) {
               exp2_poly_pair(x0, x1, p0, p1);
             } else {
               p0 = fast_exp2(x0);
