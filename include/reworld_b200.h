@@ -80,6 +80,26 @@ int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int
  * the work fills whole waves). */
 long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H);
 
+/* rw_attn_fwd for callers that cannot allocate device memory: a host runtime that
+ * owns all device memory and gives this library no allocator, or a real-time
+ * streaming loop where a cudaMalloc (which can synchronise the whole device)
+ * would stall frame delivery.  Same arguments as rw_attn_fwd without the
+ * workspace: the key-split scratch is a fixed array inside the library, of
+ * RW_ATTN_NOALLOC_SCRATCH_BYTES (80 MiB; the 704x1280 chunk shape needs about
+ * 74 MiB) of device memory that each GPU loading it keeps until the process
+ * exits.  Shapes whose scratch (rw_attn_workspace_bytes) exceeds it return
+ * RW_ERR_CAPACITY.  The first call on a device looks the array's device address
+ * up (once per device); make that first call before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race; nothing in it
+ * needs clearing between calls.  No counterpart in the reference: it is an
+ * allocation-free form of this library's own entry point. */
+#define RW_ATTN_NOALLOC_SCRATCH_BYTES (80LL * 1024 * 1024)
+int rw_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, int D,
+                        long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl,
+                        long long k_sh, long long v_sb, long long v_sl, long long v_sh, long long o_sb,
+                        long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope, int* status,
+                        void* stream);
+
 /* RoPE(+PM-RoPE) on the new chunk's K and the cache write of K and V:
  * cache_k[b, dst_start + t] = rope(k[b, t]), cache_v[b, dst_start + t] = v[b, t]
  * for t < L; optionally q_out[b, t] = rope(q_in[b, t]) when q_in != NULL.
