@@ -155,6 +155,7 @@ class Rollout:
         self.chunk = 0
         self.tot = 0
         self.launches = 0
+        self._split_cache = {}
         self.attn_events = []
 
     def fill_bank(self, n_chunks):
@@ -197,7 +198,14 @@ class Rollout:
             if self.world > 1:
                 o = head_to_seq(o, HEADS, self.group)
                 self.launches += 1
-            self.launches += 2
+            self.launches += 2 + (1 if self._split(lk) else 0)   # store, attention (+ key-split combine)
+
+    def _split(self, lk):
+        from reworld_b200 import _native
+        key = lk
+        if key not in self._split_cache:
+            self._split_cache[key] = _native.lib().rw_attn_workspace_bytes(1, CT, lk, self.H) > 0
+        return self._split_cache[key]
 
     def step(self, time_attn=False):
         for _ in range(FORWARDS_PER_CHUNK):

@@ -51,17 +51,35 @@ def a2a_unpack(blocks, H, out=None):
     return out
 
 
+def exchange_blocks(send, group=None):
+    """One all_to_all_single over a contiguous [P, ...] buffer: block p goes to
+    rank p, and block p of the result came from rank p."""
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send.contiguous(), group=group)
+    return recv
+
+
+def blocks_to_seq(recv):
+    """[P(src), B, Ls, H/P, D] received head-group blocks -> [B, P*Ls, H/P, D]
+    (source rank p holds tokens [p*Ls, (p+1)*Ls))."""
+    P, B, Ls, Hp, D = recv.shape
+    return recv.permute(1, 0, 2, 3, 4).reshape(B, P * Ls, Hp, D)
+
+
+def seq_to_blocks(x, P):
+    """[B, L, H/P, D] -> [P(dst), B, L/P, H/P, D]: block p holds rank p's tokens
+    (a view without copying when B = 1)."""
+    B, L, Hp, D = x.shape
+    return x.reshape(B, P, L // P, Hp, D).permute(1, 0, 2, 3, 4)
+
+
 def seq_to_head(x, group=None):
-    """util.all_to_all(x, scatter_dim=2, gather_dim=1): [B, L/P, H, D] -> [B, L, H/P, D]."""
+    """util.all_to_all(x, scatter_dim=2, gather_dim=1): [B, L/P, H, D] -> [B, L, H/P, D].
+    Rank r ends up with heads [r*H/P, (r+1)*H/P) for the whole sequence."""
     P = dist.get_world_size(group)
     if P == 1:
         return x
-    B, Ls, H, D = x.shape
-    send = a2a_pack(x, P)
-    recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=group)
-    # recv: [P(src), B, Ls, H/P, D] -> [B, P*Ls, H/P, D]
-    return recv.permute(1, 0, 2, 3, 4).reshape(B, P * Ls, H // P, D)
+    return blocks_to_seq(exchange_blocks(a2a_pack(x, P), group))
 
 
 def head_to_seq(x, H, group=None):
@@ -69,12 +87,7 @@ def head_to_seq(x, H, group=None):
     P = dist.get_world_size(group)
     if P == 1:
         return x
-    B, L, Hp, D = x.shape
-    Ls = L // P
-    send = x.reshape(B, P, Ls, Hp, D).permute(1, 0, 2, 3, 4).contiguous()   # no copy for B = 1
-    recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=group)
-    return a2a_unpack(recv, H)
+    return a2a_unpack(exchange_blocks(seq_to_blocks(x, P), group), H)
 
 
 def all_to_all(x, scatter_dim, gather_dim, group=None):
@@ -96,3 +109,27 @@ def distributed_attention(q, k, v, seq_lens=None, window_size=(-1, -1), group=No
     qh, kh, vh = seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group)
     x = attention(qh, kh, vh, k_lens=seq_lens, window_size=window_size)
     return head_to_seq(x, H, group)
+
+
+def sp_chunk_attention(q, k, v, cache_k, cache_v, dst_start, rope=None, group=None, out=None):
+    """One layer of the cached chunk attention under Ulysses head parallelism.
+
+    q, k, v: this rank's sequence shard [B, L/P, H, D] of the chunk (all heads);
+    cache_k / cache_v: this rank's head-resident cache [B, cap, H/P, D] (heads
+    [r*H/P, (r+1)*H/P)).  The chunk's q/k/v go seq -> head, the chunk's roped K
+    and V are written into the local cache at dst_start, the chunk's queries
+    attend cache[:, :dst_start + L] for the local heads (q's RoPE applied in the
+    kernel), and the result goes head -> seq.  Returns [B, L/P, H, D].
+    """
+    from .attention import chunk_attention
+    from .kv_cache import rope_kv_store
+    H = q.shape[2]
+    qh, kh, vh = seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group)
+    L = qh.shape[1]
+    rope_kv_store(kh, vh, cache_k, cache_v, dst_start, rope=rope)
+    o = chunk_attention(qh, cache_k[:, :dst_start + L], cache_v[:, :dst_start + L], rope=rope)
+    res = head_to_seq(o, H, group)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res

@@ -1,0 +1,72 @@
+"""Ulysses head-parallel chunk attention on 2 GPUs (one process per GPU, NCCL)
+against the single-GPU result on the same inputs: max-abs 2e-2, mean-abs 2e-3
+(only the floating-point summation order differs).  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+F, HT, WT, H = 3, 11, 20, 8            # 660-token chunk, 8 heads
+L = F * HT * WT
+N_CACHED = 3
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(1, L, H, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, L, H, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, L, H, 128, generator=g).to(torch.bfloat16)
+    ck = torch.randn(1, (N_CACHED + 1) * L, H, 128, generator=g).to(torch.bfloat16)
+    cv = torch.randn(1, (N_CACHED + 1) * L, H, 128, generator=g).to(torch.bfloat16)
+    return q, k, v, ck, cv
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, device_table
+    from reworld_b200.ulysses import sp_chunk_attention
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    q, k, v, ck, cv = _inputs()
+    Ls, Hp = L // world, H // world
+    sl = slice(rank * Ls, (rank + 1) * Ls)
+    hs = slice(rank * Hp, (rank + 1) * Hp)
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    out = sp_chunk_attention(q[:, sl].to(dev), k[:, sl].to(dev), v[:, sl].to(dev),
+                             ck[:, :, hs].contiguous().to(dev), cv[:, :, hs].contiguous().to(dev),
+                             N_CACHED * L, rope=rope)
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"r{rank}.npy"), out.float().cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ulysses_two_gpus_match_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table, rope_kv_store
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    dev = torch.device("cuda", 0)
+    q, k, v, ck, cv = _inputs()
+    ck, cv = ck.to(dev), cv.to(dev)
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    rope_kv_store(k.to(dev), v.to(dev), ck, cv, N_CACHED * L, rope=rope)
+    ref = chunk_attention(q.to(dev), ck, cv, rope=rope).float().cpu().numpy()
+    got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(2)], axis=1)
+    err = np.abs(got - ref)
+    assert err.max() < 2e-2 and err.mean() < 2e-3, (err.max(), err.mean())
