@@ -12,8 +12,9 @@ sink | recent | landmarks into all 30 layers' caches.
 
 value = attention FLOPs of the step (5 x 30 x 4*Lq*Lk*H*D) / step time, whole
 job.  With --gpus N > 1 the step runs Ulysses head-parallel (H/N heads per
-rank, sequence-sharded q/k/v exchanged by NCCL all-to-all, head-resident
-caches and bank), strong scaling.
+rank, head-resident caches and bank; the sequence-sharded q/k/v and the output
+are exchanged by this package's peer-memory scatter kernels, the RoPE and cache
+write fused into the inbound one), strong scaling.
 
 --impl reference times the reference's own CPU attention path (torch SDPA on
 the host cores, the branch wan_5b/modules/attention.py:164-179 takes without
@@ -55,7 +56,7 @@ def attn_flops(lq, lk, h):
 
 
 class Clocks:
-    """Samples nvidia-smi every 200 ms during the timed region."""
+    """Samples nvidia-smi every 50 ms during the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -69,8 +70,15 @@ class Clocks:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
+            # the timed region starts only once the sampler is producing lines
+            t0 = time.time()
+            while time.time() - t0 < 5.0:
+                self.fh.flush()
+                if os.path.getsize(self.path) > 0:
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -138,9 +146,17 @@ class Rollout:
         self.dev, self.H, self.world, self.rank, self.group = device, heads, world, rank, group
         self.cap = (BUDGET + 1) * CT
         g = torch.Generator(device=device).manual_seed(1234 + rank)
-        self.cache_k = [torch.zeros(1, self.cap, heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
-                        for _ in range(N_LAYERS)]
-        self.cache_v = [torch.zeros_like(c) for c in self.cache_k]
+        self.sp = None
+        if world > 1:
+            # head-resident caches in symmetric memory: peers write the chunk's roped K/V into them
+            from reworld_b200.ulysses import UlyssesP2P
+            self.sp = UlyssesP2P(group, N_LAYERS, self.cap, CT, HEADS, HEAD_DIM, device=device)
+            self.cache_k = [self.sp.cache_k(l) for l in range(N_LAYERS)]
+            self.cache_v = [self.sp.cache_v(l) for l in range(N_LAYERS)]
+        else:
+            self.cache_k = [torch.zeros(1, self.cap, heads, HEAD_DIM, dtype=torch.bfloat16, device=device)
+                            for _ in range(N_LAYERS)]
+            self.cache_v = [torch.zeros_like(c) for c in self.cache_k]
         # activations of the chunk per layer: sequence-sharded when world > 1
         shape = (1, seq_shard, HEADS, HEAD_DIM)
         self.q = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
@@ -178,16 +194,23 @@ class Rollout:
 
     def forward(self, time_attn=False):
         from reworld_b200 import chunk_attention, rope_kv_store
-        from reworld_b200.ulysses import head_to_seq, seq_to_head
         start_frame = (self.chunk * CT) // (TOK_H * TOK_W)
         rope = self.RopeArgs(self.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
         for l in range(N_LAYERS):
             q, k, v = self.q[l], self.k[l], self.v[l]
-            if self.world > 1:
-                q, k, v = seq_to_head(q, self.group), seq_to_head(k, self.group), seq_to_head(v, self.group)
-                self.launches += 3
-            rope_kv_store(k, v, self.cache_k[l], self.cache_v[l], self.tot, rope=rope)
             lk = self.tot + CT
+            if self.sp is not None:
+                # peer-memory exchange: scatter q/k/v (RoPE + cache write fused), barrier,
+                # attention on the local heads, scatter the output back, barrier
+                ev = None
+                if time_attn:
+                    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                self.sp.layer(l, q, k, v, self.tot, rope=rope, attn_events=ev)
+                if time_attn:
+                    self.attn_events.append((ev[0], ev[1], lk))
+                self.launches += 3 + (1 if self._split(lk) else 0)   # scatter, attention (+combine), scatter
+                continue
+            rope_kv_store(k, v, self.cache_k[l], self.cache_v[l], self.tot, rope=rope)
             if time_attn:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
@@ -195,9 +218,6 @@ class Rollout:
             if time_attn:
                 e1.record()
                 self.attn_events.append((e0, e1, lk))
-            if self.world > 1:
-                o = head_to_seq(o, HEADS, self.group)
-                self.launches += 1
             self.launches += 2 + (1 if self._split(lk) else 0)   # store, attention (+ key-split combine)
 
     def _split(self, lk):
@@ -299,6 +319,8 @@ def run_gpu(args):
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
+        ro = None                      # release the symmetric buffers before the group goes away
         dist.barrier()
         dist.destroy_process_group()
 

@@ -195,6 +195,27 @@ int rw_bank_step(rw_bank_state_t* state, int K, int protect_n, int admit, const 
 int rw_a2a_pack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
 int rw_a2a_unpack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
 
+/* Ulysses exchanges over peer memory (one sequence, B = 1), the layout
+ * transform fused in; q_dst / ck_dst / cv_dst / out_dst are DEVICE arrays of P
+ * pointers (this rank's entry is its own buffer, the others are peer-mapped).
+ * rw_sp_scatter_qkv: this rank (rank r of P) holds q, k, v [Ls, H, 128] of tokens
+ * [r*Ls, (r+1)*Ls); for head h (owner p = h / (H/P), local head hl) and chunk
+ * token t = r*Ls + s it writes q to q_dst[p] ([P*Ls, H/P, 128]) row t, RoPE(t)(k)
+ * (+ PM-RoPE when given) and v to the caches ck_dst[p] / cv_dst[p]
+ * ([cap, H/P, 128]) row dst_start + t.  Replaces the seq->head all_to_all of
+ * wan_5b/distributed/ulysses.py:40-42 (util.py:52-64) together with the RoPE and
+ * cache write of wan_5b/modules/action_model.py:265-292 on the receiving side.
+ * rw_sp_scatter_out: o [P*Ls, H/P, 128] (this rank's heads, whole chunk) ->
+ * out_dst[p] ([Ls, H, 128]) rows of rank p, heads [r*H/P, (r+1)*H/P); replaces
+ * the head->seq all_to_all of ulysses.py:54.  Cross-rank completion is the
+ * caller's barrier after each call. */
+int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, long long q_sl, long long q_sh, long long k_sl,
+                      long long k_sh, long long v_sl, long long v_sh, const unsigned long long* q_dst,
+                      const unsigned long long* ck_dst, const unsigned long long* cv_dst, int Ls, int H, int D,
+                      int P, int rank, int dst_start, int cap, const rw_rope_t* rope, void* stream);
+int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P, int rank,
+                      void* stream);
+
 /* Human-readable text of an RW_ERR_* code. */
 const char* rw_error_string(int code);
 

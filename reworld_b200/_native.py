@@ -56,6 +56,9 @@ _SIGNATURES = {
     "rw_bank_step": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp]),
     "rw_a2a_pack": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "rw_a2a_unpack": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
+    "rw_sp_scatter_qkv": (c_int, [c_vp, c_vp, c_vp] + [c_ll] * 6 + [c_vp, c_vp, c_vp] + [c_int] * 7
+                          + [ctypes.POINTER(RwRope), c_vp]),
+    "rw_sp_scatter_out": (c_int, [c_vp, c_vp] + [c_int] * 5 + [c_vp]),
     "rw_error_string": (ctypes.c_char_p, [c_int]),
     "rw_abi_version": (c_int, []),
 }

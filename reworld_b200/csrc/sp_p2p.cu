@@ -1,0 +1,141 @@
+// Ulysses exchanges over peer memory (NVLink), fused with the layout transform
+// and, on the way in, with the RoPE of k and the KV-cache write.
+//
+// Reference pattern: wan_5b/distributed/ulysses.py:17-55 (all_to_all of q, k, v
+// seq -> head, attention, all_to_all of the output head -> seq) and
+// wan_5b/distributed/util.py:52-64; the cache write and RoPE it replaces on the
+// receiving side are wan_5b/modules/action_model.py:265-292.
+//
+// Rank r holds q, k, v of tokens [r*Ls, (r+1)*Ls) of the chunk for all H heads
+// ([Ls, H, D], one sequence) and owns heads [r*Hp, (r+1)*Hp) of every cache.
+// rw_sp_scatter_qkv writes, for each (token s, head h) with p = h / Hp,
+// hl = h % Hp and t = r*Ls + s:
+//     q_dst[p][t][hl]               = q[s][h]          (RoPE of q is applied later,
+//                                                       inside the attention kernel)
+//     ck_dst[p][dst_start + t][hl]  = rope_t(k[s][h])
+//     cv_dst[p][dst_start + t][hl]  = v[s][h]
+// straight into the owning rank's buffers (plain 16-byte stores through peer
+// pointers; no multicast), so no packed staging buffer, no collective library
+// call and no separate cache-write kernel are needed.  rw_sp_scatter_out sends
+// the attention output o[t][hl] (t in [0, P*Ls)) back to rank p = t / Ls as
+// out_dst[p][t % Ls][r*Hp + hl].  Completion across ranks is signalled by the
+// caller (a stream-ordered barrier after each scatter).
+#include "common.cuh"
+#include "host_util.h"
+#include "rope.cuh"
+
+namespace rw {
+namespace sp {
+
+struct ScatterQKV {
+  const uint8_t* q;
+  const uint8_t* k;
+  const uint8_t* v;
+  long long q_sl, q_sh, k_sl, k_sh, v_sl, v_sh;
+  const unsigned long long* q_dst;
+  const unsigned long long* ck_dst;
+  const unsigned long long* cv_dst;
+  int Ls, H, Hp, P, rank, dst_start;
+  int rope_on;
+  rw_rope_t rope;
+};
+
+__global__ void __launch_bounds__(256) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
+  const long long n = (long long)p.Ls * p.H * 16;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c16 = (int)(idx & 15);
+    const long long sh = idx >> 4;
+    const int h = (int)(sh % p.H);
+    const int s = (int)(sh / p.H);
+    const int owner = h / p.Hp, hl = h - owner * p.Hp;
+    const int t = p.rank * p.Ls + s;
+    const long long eoff = (long long)c16 * 8;
+    const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + 2 * (s * p.q_sl + h * p.q_sh + eoff)));
+    uint4 kv = __ldg(reinterpret_cast<const uint4*>(p.k + 2 * (s * p.k_sl + h * p.k_sh + eoff)));
+    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(p.v + 2 * (s * p.v_sl + h * p.v_sh + eoff)));
+    if (p.rope_on) kv = rope_chunk(kv, c16, rope_token(p.rope, t, 0));
+    const long long qoff = 2 * (((long long)t * p.Hp + hl) * 128 + eoff);
+    const long long coff = 2 * (((long long)(p.dst_start + t) * p.Hp + hl) * 128 + eoff);
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.q_dst[owner]) + qoff) = qv;
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ck_dst[owner]) + coff) = kv;
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    scatter_out_kernel(const uint8_t* __restrict__ o, const unsigned long long* __restrict__ out_dst, int L, int H,
+                       int Hp, int P, int rank) {
+  const int Ls = L / P;
+  const long long n = (long long)L * Hp * 16;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c16 = (int)(idx & 15);
+    const long long th = idx >> 4;
+    const int hl = (int)(th % Hp);
+    const int t = (int)(th / Hp);
+    const int owner = t / Ls, s = t - owner * Ls;
+    const uint4 val = __ldg(reinterpret_cast<const uint4*>(o + 2 * (((long long)t * Hp + hl) * 128 + c16 * 8)));
+    const long long doff = 2 * (((long long)s * H + rank * Hp + hl) * 128 + c16 * 8);
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out_dst[owner]) + doff) = val;
+  }
+}
+
+inline unsigned grid_for(long long n) {
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace sp
+}  // namespace rw
+
+using namespace rw;
+
+extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, long long q_sl, long long q_sh,
+                                 long long k_sl, long long k_sh, long long v_sl, long long v_sh,
+                                 const unsigned long long* q_dst, const unsigned long long* ck_dst,
+                                 const unsigned long long* cv_dst, int Ls, int H, int D, int P, int rank,
+                                 int dst_start, int cap, const rw_rope_t* rope, void* stream) {
+  if (!q || !k || !v || !q_dst || !ck_dst || !cv_dst) return RW_ERR_INVALID_ARG;
+  if (D != 128) return RW_ERR_UNSUPPORTED;
+  if (Ls < 1 || H < 1 || P < 1 || (H % P) != 0 || rank < 0 || rank >= P || dst_start < 0) return RW_ERR_INVALID_ARG;
+  if ((long long)dst_start + (long long)P * Ls > cap) return RW_ERR_CAPACITY;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return RW_ERR_INVALID_ARG;
+  const long long st[6] = {q_sl, q_sh, k_sl, k_sh, v_sl, v_sh};
+  for (int i = 0; i < 6; ++i)
+    if (st[i] < 0 || (st[i] % 8) != 0) return RW_ERR_INVALID_ARG;
+  sp::ScatterQKV p{};
+  p.q = (const uint8_t*)q;
+  p.k = (const uint8_t*)k;
+  p.v = (const uint8_t*)v;
+  p.q_sl = q_sl; p.q_sh = q_sh; p.k_sl = k_sl; p.k_sh = k_sh; p.v_sl = v_sl; p.v_sh = v_sh;
+  p.q_dst = q_dst;
+  p.ck_dst = ck_dst;
+  p.cv_dst = cv_dst;
+  p.Ls = Ls;
+  p.H = H;
+  p.Hp = H / P;
+  p.P = P;
+  p.rank = rank;
+  p.dst_start = dst_start;
+  p.rope_on = 0;
+  if (rope != nullptr) {
+    if (!rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
+    p.rope = *rope;
+    p.rope_on = 1;
+  }
+  sp::scatter_qkv_kernel<<<sp::grid_for((long long)Ls * H * 16), 256, 0, (cudaStream_t)stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}
+
+extern "C" int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P,
+                                 int rank, void* stream) {
+  if (!o || !out_dst) return RW_ERR_INVALID_ARG;
+  if (D != 128) return RW_ERR_UNSUPPORTED;
+  if (L < 1 || H < 1 || P < 1 || (H % P) != 0 || (L % P) != 0 || rank < 0 || rank >= P) return RW_ERR_INVALID_ARG;
+  if (!aligned16(o)) return RW_ERR_INVALID_ARG;
+  sp::scatter_out_kernel<<<sp::grid_for((long long)L * (H / P) * 16), 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)o, out_dst, L, H, H / P, P, rank);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}

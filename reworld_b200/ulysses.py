@@ -133,3 +133,90 @@ def sp_chunk_attention(q, k, v, cache_k, cache_v, dst_start, rope=None, group=No
         out.copy_(res)
         return out
     return res
+
+
+class UlyssesP2P:
+    """Head-parallel cached chunk attention with the exchanges done by this
+    package's kernels over peer memory (NVLink) instead of a collective library.
+
+    Per layer: rw_sp_scatter_qkv (each rank writes its sequence shard's q into
+    the owning rank's q buffer and its roped k and v straight into the owning
+    rank's KV cache), a barrier, the chunk attention on the local heads over the
+    local (head-resident) cache, rw_sp_scatter_out (output rows back to the
+    ranks that own the tokens), a barrier.  The q buffer, output buffer and all
+    layers' caches are allocated as symmetric memory so every rank holds the
+    peers' device pointers.  One sequence (B = 1), as in the streaming rollout.
+    """
+
+    def __init__(self, group, n_layers, cap_tokens, chunk_tokens, heads, head_dim=128, device=None,
+                 barrier_timeout_ms=10000):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if heads % self.P or chunk_tokens % self.P:
+            raise ValueError("heads and chunk tokens must divide by the number of ranks")
+        self.H, self.Hp, self.D = heads, heads // self.P, head_dim
+        self.L, self.Ls, self.cap, self.n_layers = chunk_tokens, chunk_tokens // self.P, cap_tokens, n_layers
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.timeout_ms = barrier_timeout_ms
+        bf16 = torch.bfloat16
+        self.caches = symm.empty(n_layers, 2, cap_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
+        self.qbuf = symm.empty(chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
+        self.obuf = symm.empty(self.Ls, heads, head_dim, dtype=bf16, device=self.device)
+        self.caches.zero_()
+        self.h_c = symm.rendezvous(self.caches, group)
+        self.h_q = symm.rendezvous(self.qbuf, group)
+        self.h_o = symm.rendezvous(self.obuf, group)
+        per_tensor = cap_tokens * self.Hp * head_dim * 2
+        base = list(self.h_c.buffer_ptrs)
+        ptrs = [[[b + (l * 2 + kv) * per_tensor for b in base] for kv in range(2)] for l in range(n_layers)]
+        self.cache_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)   # [layer, k/v, P]
+        self.q_ptrs = torch.tensor(list(self.h_q.buffer_ptrs), dtype=torch.int64, device=self.device)
+        self.o_ptrs = torch.tensor(list(self.h_o.buffer_ptrs), dtype=torch.int64, device=self.device)
+        self.attn_out = torch.empty(1, chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
+
+    def cache_k(self, layer):
+        return self.caches[layer, 0].unsqueeze(0)
+
+    def cache_v(self, layer):
+        return self.caches[layer, 1].unsqueeze(0)
+
+    def scatter_qkv(self, layer, q, k, v, dst_start, rope=None):
+        """q, k, v: [1, Ls, H, D] bf16 (this rank's tokens, all heads)."""
+        import ctypes
+        lib = _native.lib()
+        rs = rope.struct() if rope is not None else None
+        code = lib.rw_sp_scatter_qkv(
+            c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()),
+            q.stride(1), q.stride(2), k.stride(1), k.stride(2), v.stride(1), v.stride(2),
+            c_vp(self.q_ptrs.data_ptr()), c_vp(self.cache_ptrs[layer, 0].data_ptr()),
+            c_vp(self.cache_ptrs[layer, 1].data_ptr()), self.Ls, self.H, self.D, self.P, self.rank,
+            int(dst_start), self.cap, ctypes.byref(rs) if rs is not None else None, _native.stream_ptr(self.device))
+        _native.check(code, "rw_sp_scatter_qkv")
+
+    def scatter_out(self, o):
+        lib = _native.lib()
+        code = lib.rw_sp_scatter_out(c_vp(o.data_ptr()), c_vp(self.o_ptrs.data_ptr()), self.L, self.H, self.D,
+                                     self.P, self.rank, _native.stream_ptr(self.device))
+        _native.check(code, "rw_sp_scatter_out")
+
+    def layer(self, layer, q, k, v, dst_start, rope=None, attn_events=None):
+        """One layer's cached chunk attention; returns [1, Ls, H, D] (this rank's
+        tokens, all heads; valid until the next call's output exchange)."""
+        from .attention import chunk_attention
+        for t in (q, k, v):
+            if t.dtype != torch.bfloat16 or t.shape != (1, self.Ls, self.H, self.D) or t.stride(-1) != 1:
+                raise ValueError("q, k, v must be bf16 [1, L/P, H, D] with a contiguous head dim")
+        self.scatter_qkv(layer, q, k, v, dst_start, rope)
+        self.h_q.barrier(channel=0, timeout_ms=self.timeout_ms)
+        lk = dst_start + self.L
+        if attn_events is not None:
+            attn_events[0].record()
+        o = chunk_attention(self.qbuf.unsqueeze(0), self.cache_k(layer)[:, :lk], self.cache_v(layer)[:, :lk],
+                            rope=rope, out=self.attn_out)
+        if attn_events is not None:
+            attn_events[1].record()
+        self.scatter_out(o[0])
+        self.h_o.barrier(channel=0, timeout_ms=self.timeout_ms)
+        return self.obuf.unsqueeze(0)

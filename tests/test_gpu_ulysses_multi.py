@@ -70,3 +70,67 @@ def test_ulysses_two_gpus_match_single_gpu(tmp_path):
     got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(2)], axis=1)
     err = np.abs(got - ref)
     assert err.max() < 2e-2 and err.mean() < 2e-3, (err.max(), err.mean())
+
+
+def _p2p_worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, device_table, _native
+    from reworld_b200.ulysses import UlyssesP2P
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    q, k, v, ck, cv = _inputs()
+    Ls, Hp = L // world, H // world
+    sl = slice(rank * Ls, (rank + 1) * Ls)
+    hs = slice(rank * Hp, (rank + 1) * Hp)
+    sp = UlyssesP2P(dist.group.WORLD, 1, (N_CACHED + 1) * L, L, H, device=dev)
+    n0 = N_CACHED * L
+    sp.cache_k(0)[:, :n0].copy_(ck[:, :n0, hs].to(dev))
+    sp.cache_v(0)[:, :n0].copy_(cv[:, :n0, hs].to(dev))
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    outs = []
+    for rep in range(2):                         # twice: buffers are reused across calls
+        out = sp.layer(0, q[:, sl].to(dev), k[:, sl].to(dev), v[:, sl].to(dev), n0, rope=rope)
+        outs.append(out.float().cpu().numpy())
+    torch.cuda.synchronize()
+    _native.check_status(dev)
+    np.save(os.path.join(out_dir, f"p2p_r{rank}.npy"), outs[-1])
+    np.save(os.path.join(out_dir, f"p2p_first_r{rank}.npy"), outs[0])
+    np.save(os.path.join(out_dir, f"p2p_k_r{rank}.npy"), sp.cache_k(0)[:, n0:n0 + L].float().cpu().numpy())
+    dist.barrier()
+    del sp
+    dist.destroy_process_group()
+
+
+def test_ulysses_p2p_two_gpus_match_single_gpu(tmp_path):
+    """Peer-memory exchanges (RoPE + cache write fused into the seq->head scatter)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table, rope_kv_store
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_p2p_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    dev = torch.device("cuda", 0)
+    q, k, v, ck, cv = _inputs()
+    ck, cv = ck.to(dev), cv.to(dev)
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    n0 = N_CACHED * L
+    rope_kv_store(k.to(dev), v.to(dev), ck, cv, n0, rope=rope)
+    ref = chunk_attention(q.to(dev), ck, cv, rope=rope).float().cpu().numpy()
+    got = np.concatenate([np.load(tmp_path / f"p2p_r{r}.npy") for r in range(2)], axis=1)
+    first = np.concatenate([np.load(tmp_path / f"p2p_first_r{r}.npy") for r in range(2)], axis=1)
+    for g in (got, first):
+        err = np.abs(g - ref)
+        assert err.max() < 2e-2 and err.mean() < 2e-3, (err.max(), err.mean())
+    # the owning ranks' caches hold the same roped K rows as the single-GPU cache (bit for bit)
+    kr = ck[:, n0:n0 + L].float().cpu().numpy()
+    Hp = H // 2
+    for r in range(2):
+        np.testing.assert_array_equal(np.load(tmp_path / f"p2p_k_r{r}.npy"), kr[:, :, r * Hp:(r + 1) * Hp])
