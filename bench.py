@@ -64,6 +64,7 @@ class Clocks:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.skip = 0
         self.path = tempfile.mktemp(suffix=".csv")
 
     def __enter__(self):
@@ -79,6 +80,8 @@ class Clocks:
                 if os.path.getsize(self.path) > 0:
                     break
                 time.sleep(0.02)
+            time.sleep(0.06)
+            self.skip = sum(1 for _ in open(self.path))   # lines sampled before the timed region
         except Exception:
             self.proc = None
         return self
@@ -96,7 +99,9 @@ class Clocks:
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
-        for line in open(self.path):
+        for i, line in enumerate(open(self.path)):
+            if i < self.skip:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 rows.append(parts)
