@@ -212,92 +212,114 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
-    // A single thread issues both query tiles' MMAs in the strict alternation
+    // One thread (lane 0) issues both query tiles' MMAs in the strict alternation
     // PV0(j-1), QK0(j), PV1(j-1), QK1(j): each softmax warpgroup then has the
     // other tile's two GEMMs of time to turn its S tile into P.  Per key tile it
     // commits three times: S0 ready, S1 ready, and step_free (K_j and V_{j-1}
     // no longer read), which the producer waits on before refilling those slots.
+    // The whole warp runs the loop and every wait (warp-uniform control flow), so
+    // the descriptors below stay warp-uniform values; lane 0 alone issues, always
+    // the same thread, because a commit tracks the MMAs of the thread issuing it.
     setmaxnreg_dec_72();
-    if (lane == 0) {
-      constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
-      constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, HD, 0, 1);  // P from TMEM, V MN-major
-      const uint32_t q_addr[2] = {smem_u32(smem_q[0]), smem_u32(smem_q[1])};
-      const uint32_t ring_addr = smem_u32(smem_ring);
-      bool ok = mbar_wait(&sb.q_ready[0], 0, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
-      if (ok && has_q1) ok = mbar_wait(&sb.q_ready[1], 0, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
-      tc_fence_after();
+    constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
+    constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, HD, 0, 1);  // P from TMEM, V MN-major
+    // Descriptor bases.  A byte offset d within the same buffer is added as d >> 4
+    // to the start-address field (bits 0-13): shared addresses stay below 256 KB,
+    // so the field never carries into the next one.
+    const uint64_t dq0 = umma_desc(smem_u32(smem_q[0]), 16, 1024), dq1 = umma_desc(smem_u32(smem_q[1]), 16, 1024);
+    const uint64_t dk_ring = umma_desc(smem_u32(smem_ring), 16, 1024);          // K tiles, K-major
+    const uint64_t dv_ring = umma_desc(smem_u32(smem_ring), HALF_BYTES, 1024);  // V tiles, MN-major
+    constexpr uint64_t SLOT_DESC = TILE_BYTES >> 4;
+    const bool leader = lane == 0;
 
-      auto issue_qk = [&](int i, uint32_t k_addr) {
+    const uint32_t ts0 = tmem + tcol_s(0), ts1 = tmem + tcol_s(1), to0 = tmem + tcol_o(0), to1 = tmem + tcol_o(1);
+    auto issue_qk = [](uint32_t ts, uint64_t dq, uint64_t dk) {
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + tcol_s(i), umma_desc(q_addr[i] + off, 16, 1024), umma_desc(k_addr + off, 16, 1024),
-                 IDESC_QK, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int i, uint32_t v_addr, bool acc) {
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint64_t off = (uint64_t)(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4);
+        mma_ss(ts, dq + off, dk + off, IDESC_QK, kk > 0 ? 1u : 0u);
+      }
+    };
+    auto issue_pv = [](uint32_t to, uint32_t ts, uint64_t dv, bool acc) {
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ts(tmem + tcol_o(i), tmem + tcol_s(i) + kk * 8, umma_desc(v_addr + kk * 2048, HALF_BYTES, 1024),
-                 IDESC_PV, (acc || kk > 0) ? 1u : 0u);
-      };
+      for (int kk = 0; kk < BN / 16; ++kk)
+        mma_ts(to, ts + kk * 8, dv + (uint64_t)((kk * 2048) >> 4), IDESC_PV, (acc || kk > 0) ? 1u : 0u);
+    };
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return warp_wait(bar, parity, sb, p.status, RW_STATUS_TIMEOUT_MMA);
+    };
 
-      // ring position of K_j (use 2j) and V_j (use 2j+1), advanced incrementally
-      uint32_t sK = 0, parK = 0, sV = 1, parV = 0;
-      uint32_t v_prev_slot = 0, v_prev_par = 0;
-      uint32_t fs = 0, fpar = 0;  // step_free barrier of key tile j
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
-        if (j > 0) {
-          if (!(ok = mbar_wait(&sb.p_ready[0], (j - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
-          if (!(ok = mbar_wait(&sb.slot_full[v_prev_slot], v_prev_par, &sb.abort_flag, p.status,
-                               RW_STATUS_TIMEOUT_MMA)))
-            break;
-          tc_fence_after();
-          issue_pv(0, vp_addr, j > 1);
-        }
-        if (!(ok = mbar_wait(&sb.slot_full[sK], parK, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA))) break;
-        const uint32_t k_addr = ring_addr + sK * TILE_BYTES;
-        issue_qk(0, k_addr);
+    bool ok = wait(&sb.q_ready[0], 0);
+    if (ok && has_q1) ok = wait(&sb.q_ready[1], 0);
+    tc_fence_after();
+    // ring position of K_j (use 2j) and V_j (use 2j+1), advanced incrementally
+    uint32_t sK = 0, parK = 0, sV = 1, parV = 0;
+    uint32_t v_prev_slot = 0, v_prev_par = 0;
+    uint32_t fs = 0;  // step_free barrier of key tile j
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const uint64_t dv_prev = dv_ring + v_prev_slot * SLOT_DESC;
+      if (j > 0) {
+        if (!(ok = wait(&sb.p_ready[0], (j - 1) & 1))) break;
+        if (!(ok = wait(&sb.slot_full[v_prev_slot], v_prev_par))) break;
+        tc_fence_after();
+        if (leader) issue_pv(to0, ts0, dv_prev, j > 1);
+        __syncwarp();
+      }
+      if (!(ok = wait(&sb.slot_full[sK], parK))) break;
+      const uint64_t dk = dk_ring + sK * SLOT_DESC;
+      if (leader) {
+        issue_qk(ts0, dq0, dk);
         tc_commit(&sb.s_full[0]);
-        if (has_q1) {
-          if (j > 0) {
-            if (!(ok = mbar_wait(&sb.p_ready[1], (j - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA)))
-              break;
-            tc_fence_after();
-            issue_pv(1, vp_addr, j > 1);
-          }
-          issue_qk(1, k_addr);
+      }
+      __syncwarp();
+      if (has_q1) {
+        if (j > 0) {
+          if (!(ok = wait(&sb.p_ready[1], (j - 1) & 1))) break;
+          tc_fence_after();
+          if (leader) issue_pv(to1, ts1, dv_prev, j > 1);
+          __syncwarp();
+        }
+        if (leader) {
+          issue_qk(ts1, dq1, dk);
           tc_commit(&sb.s_full[1]);
         }
-        tc_commit(&sb.step_free[fs]);  // K_j and V_{j-1} released once everything above completes
-        if (++fs == NSTEPBAR) { fs = 0; fpar ^= 1; }
-        v_prev_slot = sV;
-        v_prev_par = parV;
-        sK += 2;
-        if (sK >= NSLOT) { sK -= NSLOT; parK ^= 1; }
-        sV += 2;
-        if (sV >= NSLOT) { sV -= NSLOT; parV ^= 1; }
+        __syncwarp();
       }
+      if (leader) tc_commit(&sb.step_free[fs]);  // K_j and V_{j-1} released once everything above completes
+      __syncwarp();
+      if (++fs == NSTEPBAR) fs = 0;
+      v_prev_slot = sV;
+      v_prev_par = parV;
+      sK += 2;
+      if (sK >= NSLOT) { sK -= NSLOT; parK ^= 1; }
+      sV += 2;
+      if (sV >= NSLOT) { sV -= NSLOT; parV ^= 1; }
+    }
+    if (ok) {
+      const uint64_t dv_prev = dv_ring + v_prev_slot * SLOT_DESC;
+      ok = wait(&sb.p_ready[0], (n_kv - 1) & 1) && wait(&sb.slot_full[v_prev_slot], v_prev_par);
       if (ok) {
-        const uint32_t vp_addr = ring_addr + v_prev_slot * TILE_BYTES;
-        ok = mbar_wait(&sb.p_ready[0], (n_kv - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA) &&
-             mbar_wait(&sb.slot_full[v_prev_slot], v_prev_par, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
-        if (ok) {
-          tc_fence_after();
-          issue_pv(0, vp_addr, n_kv > 1);
+        tc_fence_after();
+        if (leader) {
+          issue_pv(to0, ts0, dv_prev, n_kv > 1);
           tc_commit(&sb.o_done[0]);
-          if (has_q1) {
-            ok = mbar_wait(&sb.p_ready[1], (n_kv - 1) & 1, &sb.abort_flag, p.status, RW_STATUS_TIMEOUT_MMA);
-            if (ok) {
-              tc_fence_after();
-              issue_pv(1, vp_addr, n_kv > 1);
+        }
+        __syncwarp();
+        if (has_q1) {
+          ok = wait(&sb.p_ready[1], (n_kv - 1) & 1);
+          if (ok) {
+            tc_fence_after();
+            if (leader) {
+              issue_pv(to1, ts1, dv_prev, n_kv > 1);
               tc_commit(&sb.o_done[1]);
             }
+            __syncwarp();
           }
         }
       }
-      // All MMAs issued by this thread complete before teardown.
+    }
+    // All MMAs issued by lane 0 complete before teardown.
+    if (leader) {
       tc_commit(&sb.drain);
       mbar_wait_drain(&sb.drain, 0);
     }
@@ -372,9 +394,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + 32 * c, o);
           }
         }
-        // P = 2^(s*scale_log2 - m*scale_log2): every other column pair on MUFU (ex2),
-        // the rest on the FMA pipe (exp2_poly_pair), so neither pipe limits the
-        // tile; the exponent arguments and the row sum use packed fp32x2 math.
+        // P = 2^(s*scale_log2 - m*scale_log2): three column pairs in eight on the FMA
+        // pipe (exp2_poly_pair), the rest on MUFU (ex2), which balances the two
+        // pipes (one MUFU ex2 costs a warp 8 issue cycles of that pipe, a polynomial
+        // pair about 16 of the FMA pipe); the exponent arguments and the row sum use
+        // packed fp32x2 math.
         const float nm = -m_used * sl2;
         const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
 #pragma unroll
@@ -389,7 +413,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t xv = ffma2(sv, sl2x2, nmx2);
             float x0, x1, p0, p1;
             f2_unpack(xv, x0, x1);
-            if ((e & 1) == 1) {
+            if ((0x4A >> (e & 7)) & 1) {
               exp2_poly_pair(x0, x1, p0, p1);
             } else {
               p0 = fast_exp2(x0);
