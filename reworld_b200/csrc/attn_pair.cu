@@ -1,0 +1,614 @@
+// Chunk attention forward for sm_100a on CTA pairs: o = softmax(q k^T * scale) v,
+// non-causal, bf16 in/out, fp32 accumulation in tensor memory.  Same contract as
+// attn_fwd.cu (the reference call it replaces: wan_5b/modules/action_model.py:302
+// -> wan_5b/modules/attention.py:133-179; optional 3-D RoPE + PM-RoPE phase of q,
+// causal_model.py:156-184 / action_model.py:40-51, applied in shared memory).
+//
+// A cluster of two CTAs (a pair, one per SM) owns 256 query rows of one
+// (batch, head); each CTA holds 128 of them.  The even CTA issues 2-SM
+// tcgen05.mma (cta_group::2, M = 256): A rows come from each CTA's own Q tile /
+// TMEM, the B operand is split between the two CTAs (keys [0, 64) / [64, 128) of
+// a K tile, head dims [0, 64) / [64, 128) of a V tile), and each CTA's TMEM
+// receives its own 128 rows.  Each CTA therefore loads half of every K and V
+// tile (the pair reads each tile once, like one CTA with 256 rows) and its TMEM
+// only holds 128 rows, which leaves room for three S buffers:
+//   TMEM columns  O [0,128)  S0 [128,256)  S1 [256,384)  S2 [384,512)
+// so QK^T of key tile j+3 runs while the softmax of tile j is still working and
+// the tensor pipe never waits for one softmax in a serial chain.  P_j (bf16
+// pairs) overwrites the first 64 columns of its S buffer.
+//
+// Warps (per CTA): two softmax warpgroups (warps 4w..4w+3 handle the key tiles
+// j = w mod 2; one query row per thread), warp 8 TMA producer, warp 9 MMA issuer
+// (even CTA) and TMEM owner (both CTAs, 2-SM allocation), warps 10-11 idle.
+// Key tile j lands in S buffer j mod 3, so the QK^T of tile j + 3 can run while
+// tiles j + 1 and j + 2 are in softmax.
+// MMA order (single issuing thread): QK(0), QK(1), QK(2), then for every key tile
+// j: PV(j), QK(j+3).  The softmax warpgroups pass the running row maximum of
+// tile j to the one handling j+1 through shared memory; when the maximum grows
+// by more than 2^8 (log2 units) the warpgroup rescales O in TMEM after PV(j-1)
+// completed and before publishing P(j); otherwise the stale exponent base is
+// kept (exact after the final division).  Each warpgroup keeps its own partial
+// row sum, rebased when the shared maximum changes; the two are merged at the end.
+#include "common.cuh"
+#include "host_util.h"
+#include "rope.cuh"
+
+namespace rw {
+namespace pair {
+
+constexpr int BM = 128;                      // query rows per CTA (256 per pair)
+constexpr int BN = 128;                      // keys per key tile
+constexpr int HD = 128;                      // head dim
+constexpr int NSBUF = 3;                     // S buffers in TMEM
+constexpr int NSTAGE = 4;                    // K/V stages per CTA
+constexpr int Q_BYTES = BM * HD * 2;         // 32 KB
+constexpr int Q_HALF = Q_BYTES / 2;          // 128 rows x 64 dims (one TMA box)
+constexpr int HALF_TILE = 16384;             // 64 keys x 128 dims (K half) or 128 keys x 64 dims (V half)
+constexpr int K_BOX = 8192;                  // 64 keys x 64 dims
+constexpr int PRE_BYTES = NSBUF * HALF_TILE; // K halves of key tiles 0-2 (the first QKs)
+constexpr int STAGE_BYTES = 2 * HALF_TILE;   // stage j: V half of key tile j, then K half of key tile j + 3
+constexpr int NWG = 2;                       // softmax warpgroups (key tiles j = w mod NWG)
+constexpr int NUM_THREADS = 128 * (NWG + 1);
+constexpr int SMEM_BYTES = Q_BYTES + PRE_BYTES + NSTAGE * STAGE_BYTES + 1024;
+constexpr int WARP_LOAD = 4 * NWG;
+constexpr int WARP_MMA = 4 * NWG + 1;
+constexpr int SOFTMAX_THREADS = 128 * NWG;
+// Registers: the launch gives 168 per thread (384 x 168 = 64512); the producer /
+// MMA warpgroup keeps 72 and the softmax warpgroups take 216: 128 x 72 + 256 x 216.
+// (Three softmax warpgroups at 152 registers measured 4 % slower: the softmax
+// latency rose with three warps per SMSP competing for MUFU / FMA / ALU.)
+constexpr int REG_SOFTMAX = 216;
+constexpr int REG_OTHER = 72;
+static_assert(NWG * 128 * REG_SOFTMAX + 128 * REG_OTHER <= 65536, "register split exceeds the register file");
+constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
+__host__ __device__ constexpr uint32_t tcol_o() { return 0u; }
+__host__ __device__ constexpr uint32_t tcol_s(int b) { return 128u + 128u * (uint32_t)b; }
+
+// Work split, as in attn_fwd.cu but per pair: a unit is one (batch, head,
+// 256-row query block) over all keys; n_whole units run whole, the n_tail
+// remaining ones are cut into `splits` key ranges whose unnormalised partial
+// results (O, m, l; fp32) go to the scratch slots merged by combine_kernel (attn_fwd.cu).
+struct Params {
+  int B, Lq, Lk, H;
+  int nqp;
+  int n_whole, n_tail, splits;
+  float scale_log2;
+  int rope_on;
+  rw_rope_t rope;
+  int* status;
+  float* scratch;
+};
+
+constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
+
+struct __align__(8) Barriers {
+  uint64_t pre_full;             // even CTA: both CTAs' K halves of key tiles 0-2 landed
+  uint64_t stage_full[NSTAGE];   // even CTA: both CTAs' halves of the stage landed
+  uint64_t stage_free[NSTAGE];   // both: PV(j) and QK(j+3) reading stage j completed
+  uint64_t q_full;               // own Q tile landed
+  uint64_t q_ready;              // even CTA: both Q tiles RoPE'd (2 x 256 arrivals)
+  uint64_t s_full[NSBUF];        // both: S of the buffer's current key tile complete
+  uint64_t p_ready[NSBUF];       // even CTA: P written in both CTAs (2 x 128 arrivals)
+  uint64_t m_ready[NSBUF];       // own: running maximum of a key tile published (128 arrivals)
+  uint64_t o_done;            // both: last PV complete
+  uint64_t epi;               // own: output rows staged in shared memory (256 arrivals)
+  uint64_t drain;             // even CTA: every MMA complete
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Ctx {
+  Barriers* sb;
+  uint32_t peer_abort;  // shared::cluster address of the peer's abort flag
+  int* status;
+};
+
+// Bounded wait; on expiry raises this CTA's and the peer's abort flags and
+// records `err` in the status word.
+__device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, const Ctx& c, int err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0u) {
+      if (*(volatile int*)&c.sb->abort_flag) return false;
+      if (globaltimer_ns() - t0 > RW_WAIT_TIMEOUT_NS) {
+        c.sb->abort_flag = 1;
+        st_shared_cluster_u32(c.peer_abort, 1u);
+        report_status(c.status, err);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool pwait_warp(uint64_t* bar, uint32_t parity, const Ctx& c, int err) {
+  const bool ok = pwait(bar, parity, c, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// RoPE of head dims [64 h, 64 h + 64) of one row of the 128-byte-swizzled Q tile.
+__device__ __forceinline__ void rope_row_half(uint8_t* tile, int r, int h, int token, int b, const rw_rope_t& rp) {
+  const RopeToken rt = rope_token(rp, token, b);
+  if (!rt.on) return;
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    uint4* ptr = reinterpret_cast<uint4*>(tile + h * Q_HALF + r * 128 + ((c ^ (r & 7)) << 4));
+    *ptr = rope_chunk(*ptr, 8 * h + c, rt);
+  }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    attn_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                     const __grid_constant__ Params p) {
+  extern __shared__ uint8_t dsmem_raw[];
+  __shared__ Barriers sb;
+  __shared__ float m_sh[NSBUF][BM];    // running maximum handed from key tile j to j + 1
+  __shared__ float fin[2 * NWG][BM];   // per warpgroup: exponent base and partial row sum
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_q = smem;
+  uint8_t* pre = smem + Q_BYTES;
+  uint8_t* stages = pre + PRE_BYTES;
+
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
+  const int lane = threadIdx.x & 31;
+  const int n_kv_all = (p.Lk + BN - 1) / BN;
+  const int kv_tail = p.Lk - (n_kv_all - 1) * BN;
+  const int pair_id = blockIdx.x >> 1;
+  int unit, kv0, kv1, slot = -1;
+  if (pair_id < p.n_whole) {
+    unit = pair_id;
+    kv0 = 0;
+    kv1 = n_kv_all;
+  } else {
+    const int t = pair_id - p.n_whole;
+    const int e = t % p.n_tail, piece = t / p.n_tail;
+    unit = p.n_whole + e;
+    kv0 = (int)((long long)piece * n_kv_all / p.splits);
+    kv1 = (int)((long long)(piece + 1) * n_kv_all / p.splits);
+    slot = e * p.splits + piece;
+  }
+  const int qp = unit % p.nqp;
+  const int head = (unit / p.nqp) % p.H;
+  const int bidx = unit / (p.nqp * p.H);
+  const int row0 = qp * (2 * BM) + (int)rank * BM;  // this CTA's first query row
+  const int n_kv = kv1 - kv0;
+
+  if (threadIdx.x == WARP_LOAD * 32) {
+    mbar_init(&sb.pre_full, 1);
+    for (int t = 0; t < NSTAGE; ++t) {
+      mbar_init(&sb.stage_full[t], 1);
+      mbar_init(&sb.stage_free[t], 1);
+    }
+    mbar_init(&sb.q_full, 1);
+    mbar_init(&sb.q_ready, 2 * 256);
+    for (int b = 0; b < NSBUF; ++b) {
+      mbar_init(&sb.s_full[b], 1);
+      mbar_init(&sb.p_ready[b], 2 * BM);
+    }
+    for (int b = 0; b < NSBUF; ++b) mbar_init(&sb.m_ready[b], BM);
+    mbar_init(&sb.o_done, 1);
+    mbar_init(&sb.epi, 256);
+    mbar_init(&sb.drain, 1);
+    sb.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc_pair(&sb.tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+  const Ctx cx{&sb, mapa_shared(smem_u32(&sb.abort_flag), rank ^ 1u), p.status};
+
+  if (warp == WARP_LOAD) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    setmaxnreg_dec<REG_OTHER>();
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      const uint64_t pol = l2_policy_evict_last();  // K/V tiles are re-read by the other query pairs of the head
+      mbar_expect_tx(&sb.q_full, Q_BYTES);
+      tma_load_4d(smem_q, &tm_q, &sb.q_full, 0, head, row0, bidx);
+      tma_load_4d(smem_q + Q_HALF, &tm_q, &sb.q_full, 64, head, row0, bidx);
+      bool ok = true;
+      const int k_off = 64 * (int)rank;  // this CTA's keys of a K tile / head dims of a V tile
+      auto load_k = [&](uint8_t* dst, uint32_t bar, int kt) {
+        const int key0 = (kv0 + kt) * BN + k_off;
+        tma_load_4d_pair(dst, &tm_k, bar, 0, head, key0, bidx, pol);
+        tma_load_4d_pair(dst + K_BOX, &tm_k, bar, 64, head, key0, bidx, pol);
+      };
+      const int n_pre = n_kv < NSBUF ? n_kv : NSBUF;
+      if (even) mbar_expect_tx(&sb.pre_full, 2 * HALF_TILE * n_pre);
+      const uint32_t pre_bar = mapa_shared(smem_u32(&sb.pre_full), 0);
+      for (int kt = 0; kt < n_pre; ++kt) load_k(pre + kt * HALF_TILE, pre_bar, kt);
+      for (int j = 0; j < n_kv; ++j) {
+        const int t = j % NSTAGE;
+        if (j >= NSTAGE && !(ok = pwait(&sb.stage_free[t], (uint32_t)(j / NSTAGE - 1) & 1u, cx, RW_STATUS_TIMEOUT_LOAD)))
+          break;
+        const bool has_k = j + NSBUF < n_kv;
+        if (even) mbar_expect_tx(&sb.stage_full[t], 2 * HALF_TILE * (has_k ? 2 : 1));
+        const uint32_t bar = mapa_shared(smem_u32(&sb.stage_full[t]), 0);
+        uint8_t* st = stages + t * STAGE_BYTES;
+        tma_load_4d_pair(st, &tm_v, bar, k_off, head, (kv0 + j) * BN, bidx, pol);
+        if (has_k) load_k(st + HALF_TILE, bar, j + NSBUF);
+      }
+      // The even CTA sees every issued copy of the pair complete on its barriers
+      // (already consumed by the MMA issuer on the normal path).
+      if (even) {
+        mbar_wait_drain(&sb.pre_full, 0);
+        const int first = n_kv > NSTAGE ? n_kv - NSTAGE : 0;
+        for (int j = first; j < n_kv; ++j) mbar_wait_drain(&sb.stage_full[j % NSTAGE], (uint32_t)(j / NSTAGE) & 1u);
+      }
+      mbar_wait_drain(&sb.q_full, 0);
+    }
+    __syncwarp();
+  } else if (warp == WARP_MMA) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    setmaxnreg_dec<REG_OTHER>();
+    if (even) {
+      constexpr uint32_t IDESC_QK = idesc_bf16_f32(2 * BM, BN, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t IDESC_PV = idesc_bf16_f32(2 * BM, HD, 0, 1);  // P from TMEM, V MN-major
+      // Descriptor bases; a byte offset d within a buffer is added as d >> 4 (the
+      // start-address field never carries: shared addresses stay below 256 KB).
+      const uint64_t dq = umma_desc(smem_u32(smem_q), 16, 1024);
+      const uint64_t dk_pre = umma_desc(smem_u32(pre), 16, 1024);             // K halves: 64 keys, K-major
+      const uint64_t dv_st = umma_desc(smem_u32(stages), 16384, 1024);        // V halves: 64 dims, MN-major
+      const uint64_t dk_st = umma_desc(smem_u32(stages + HALF_TILE), 16, 1024);
+      constexpr uint64_t PRE_DESC = HALF_TILE >> 4, STAGE_DESC = STAGE_BYTES >> 4;
+      auto issue_qk = [](uint32_t ts, uint64_t dqa, uint64_t dkb) {
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t oa = (uint64_t)(((kk >> 2) * Q_HALF + (kk & 3) * 32) >> 4);
+          const uint64_t ob = (uint64_t)(((kk >> 2) * K_BOX + (kk & 3) * 32) >> 4);
+          mma_ss_pair(ts, dqa + oa, dkb + ob, IDESC_QK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [](uint32_t to, uint32_t ts, uint64_t dvb, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts_pair(to, ts + kk * 8, dvb + (uint64_t)((kk * 2048) >> 4), IDESC_PV, (acc || kk > 0) ? 1u : 0u);
+      };
+      // Per key tile the issuer waits twice (P ready, stage landed) and commits
+      // twice (S of tile j + 3 ready, stage j free): waits and commits cost ~100
+      // clocks each and an MMA issue ~50, so one thread keeps up with 1024
+      // clocks of tensor work per key tile only with this little bookkeeping.
+      bool ok = pwait_warp(&sb.q_ready, 0, cx, RW_STATUS_TIMEOUT_MMA) &&
+                pwait_warp(&sb.pre_full, 0, cx, RW_STATUS_TIMEOUT_MMA);
+      tc_fence_after();
+      if (ok) {
+        const int n_pre = n_kv < NSBUF ? n_kv : NSBUF;
+        if (elect_one()) {
+          for (int kt = 0; kt < n_pre; ++kt) {
+            issue_qk(tmem + tcol_s(kt), dq, dk_pre + kt * PRE_DESC);
+            tc_commit_pair_mc(&sb.s_full[kt], 0x3);
+          }
+        }
+        __syncwarp();
+      }
+      int b = 0, t = 0;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (!(ok = pwait_warp(&sb.p_ready[b], (uint32_t)(j / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
+        if (!(ok = pwait_warp(&sb.stage_full[t], (uint32_t)(j / NSTAGE) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          issue_pv(tmem + tcol_o(), tmem + tcol_s(b), dv_st + t * STAGE_DESC, j > 0);
+          if (j == n_kv - 1) tc_commit_pair_mc(&sb.o_done, 0x3);
+          if (j + NSBUF < n_kv) {
+            // S buffer b is free again in pipe order: PV(j) reads P(j) before QK(j+3) writes it.
+            issue_qk(tmem + tcol_s(b), dq, dk_st + t * STAGE_DESC);
+            tc_commit_pair_mc(&sb.s_full[b], 0x3);
+          }
+          tc_commit_pair_mc(&sb.stage_free[t], 0x3);
+        }
+        __syncwarp();
+        if (++b == NSBUF) b = 0;
+        if (++t == NSTAGE) t = 0;
+      }
+      if (elect_one()) {
+        tc_commit_pair_mc(&sb.drain, 0x1);
+        mbar_wait_drain(&sb.drain, 0);
+      }
+      __syncwarp();
+    }
+  } else if (warp < 4 * NWG) {
+    // ------------------------------------------------------------ softmax + epilogue (both CTAs)
+    setmaxnreg_inc<REG_SOFTMAX>();
+    const int w = warp >> 2;  // key tiles j = w mod NWG
+    const int r = threadIdx.x & 127;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tO = tmem + lane_base + tcol_o();
+    const float sl2 = p.scale_log2;
+    const uint32_t p_ready_cl0 = mapa_shared(smem_u32(&sb.p_ready[0]), 0);
+    bool ok = pwait_warp(&sb.q_full, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX);
+    if (ok && w < 2) {
+      if (p.rope_on) rope_row_half(smem_q, r, w, row0 + r, bidx, p.rope);
+      fence_proxy_async_smem();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&sb.q_ready), 0));
+    }
+    float m_base = -INFINITY;  // exponent base of this warpgroup's partial row sum
+    uint64_t l2 = 0ull;        // packed (even-column, odd-column) partial row sums
+    for (int j = w; j < n_kv && ok; j += NWG) {
+      const int b = j % NSBUF;  // S buffer of key tile j
+      const uint32_t tS = tmem + lane_base + tcol_s(b);
+      if (!(ok = pwait_warp(&sb.s_full[b], (uint32_t)(j / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX))) break;
+      tc_fence_after();
+      const bool tail = kv0 + j == n_kv_all - 1 && kv_tail < BN;
+      // pass 1: row maximum, 64 columns at a time (registers are kept for pass 2)
+      float row_max = -INFINITY;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld32(tS + 64 * hh, sr[0]);
+        tmem_ld32(tS + 64 * hh + 32, sr[1]);
+        tmem_wait_ld();
+        reg_fence32(sr[0]);
+        reg_fence32(sr[1]);
+        if (tail) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (64 * hh + 32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float a = fmax3(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]), __uint_as_float(sr[c][2]));
+#pragma unroll
+          for (int e = 3; e + 1 < 32; e += 2) a = fmax3(a, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+          row_max = fmax3(row_max, a, __uint_as_float(sr[c][31]));
+        }
+      }
+      // running maximum after key tile j - 1, from the warpgroup that handled it
+      float m_prev = -INFINITY;
+      if (j > 0) {
+        const int jp = j - 1;
+        if (!(ok = pwait_warp(&sb.m_ready[jp % NSBUF], (uint32_t)(jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
+          break;
+        m_prev = m_sh[jp % NSBUF][r];
+      }
+      const float m_new = fmaxf(m_prev, row_max);
+      const bool need = (m_new - m_prev) * sl2 > RESCALE_THRESHOLD;
+      const float m_use = need ? m_new : m_prev;
+      m_sh[b][r] = m_use;
+      mbar_arrive(&sb.m_ready[b]);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds tiles < j relative to m_prev: rescale it once PV(j-1) has landed
+        // (PV(j) is issued only after this warpgroup publishes P(j)).
+        const float alpha = need ? fast_exp2((m_prev - m_use) * sl2) : 1.f;
+        // stage_free of key tile j - 1 is committed after PV(j-1)
+        if (!(ok = pwait_warp(&sb.stage_free[(j - 1) % NSTAGE], (uint32_t)((j - 1) / NSTAGE) & 1u, cx,
+                              RW_STATUS_TIMEOUT_SOFTMAX)))
+          break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + 32 * c, o);
+        }
+      }
+      if (m_base != m_use) {  // rebase this warpgroup's partial sum (0 while it is empty)
+        float l_lo, l_hi;
+        f2_unpack(l2, l_lo, l_hi);
+        const float f = fast_exp2((m_base - m_use) * sl2);
+        l2 = f2_pack(l_lo * f, l_hi * f);
+        m_base = m_use;
+      }
+      // pass 2: P = 2^(s*scale_log2 - m*scale_log2) for columns [64 h, 64 h + 64),
+      // three column pairs in eight on the FMA pipe (exp2_poly_pair), the rest on
+      // MUFU (ex2).  P (bf16 pairs) goes to columns [32 h, 32 h + 32) of the
+      // buffer: S columns already read.
+      const float nm = -m_use * sl2;
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sr[2][32];
+        tmem_ld32(tS + 64 * h, sr[0]);
+        tmem_ld32(tS + 64 * h + 32, sr[1]);
+        tmem_wait_ld();
+        reg_fence32(sr[0]);
+        reg_fence32(sr[1]);
+        if (tail) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (64 * h + 32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
+        }
+        uint32_t pk[32];
+        uint64_t lacc[2] = {0ull, 0ull};
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const uint64_t sv = f2_pack(__uint_as_float(sr[e >> 4][(2 * e) & 31]),
+                                      __uint_as_float(sr[e >> 4][(2 * e + 1) & 31]));
+          const uint64_t xv = ffma2(sv, sl2x2, nmx2);
+          float x0, x1, p0, p1;
+          f2_unpack(xv, x0, x1);
+          if ((0x4A >> (e & 7)) & 1) {
+            exp2_poly_pair(x0, x1, p0, p1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          lacc[e & 1] = fadd2(lacc[e & 1], f2_pack(p0, p1));
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        l2 = fadd2(l2, fadd2(lacc[0], lacc[1]));
+        tmem_st32(tS + 32 * h, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive_cluster(p_ready_cl0 + 8u * (uint32_t)b);
+    }
+    // ---- merge the three partial row sums; epilogue (warpgroups 0 and 1)
+    {
+      float l_lo, l_hi;
+      f2_unpack(l2, l_lo, l_hi);
+      fin[2 * w][r] = m_base;
+      fin[2 * w + 1][r] = l_lo + l_hi;
+    }
+    named_bar_sync(1, SOFTMAX_THREADS);
+    float m_fin = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < NWG; ++g) m_fin = fmaxf(m_fin, fin[2 * g][r]);
+    float l_row = 0.f;
+#pragma unroll
+    for (int g = 0; g < NWG; ++g) {
+      const float lg = fin[2 * g + 1][r];
+      if (lg > 0.f) l_row += lg * fast_exp2((fin[2 * g][r] - m_fin) * sl2);
+    }
+    ok = __all_sync(0xffffffffu, ok) && !*(volatile int*)&sb.abort_flag;
+    if (ok && w < 2) ok = pwait_warp(&sb.o_done, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX);
+    if (ok && w < 2 && slot >= 0) {
+      // partial key range: unnormalised O columns [64 w, 64 w + 64) (column-major),
+      // the exponent base and the row sum, for combine_kernel
+      tc_fence_after();
+      float* base = p.scratch + (size_t)slot * SLOT_FLOATS;
+      const int row = (int)rank * BM + r;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 64 * w + 32 * c, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) base[(size_t)(64 * w + 32 * c + e) * 256 + row] = __uint_as_float(o[e]);
+      }
+      if (w == 0) {
+        base[128 * 256 + row] = m_fin;
+        base[128 * 256 + 256 + row] = l_row;
+      }
+    } else if (ok && w < 2) {
+      // whole unit: O / l -> bf16 -> shared memory (reusing the Q tile; every QK
+      // completed before o_done) -> TMA store; warpgroup w writes box w
+      tc_fence_after();
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 64 * w + 32 * c, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = c * 4 + q;
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+          v.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+          v.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+          v.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+          *reinterpret_cast<uint4*>(smem_q + w * Q_HALF + r * 128 + ((chunk ^ (r & 7)) << 4)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&sb.epi);
+      if (threadIdx.x == 0) {
+        if (pwait(&sb.epi, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX)) {
+          tma_store_4d(&tm_o, smem_q, 0, head, row0, bidx);
+          tma_store_4d(&tm_o, smem_q + Q_HALF, 64, head, row0, bidx);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();
+        }
+      }
+    }
+  } else {
+    setmaxnreg_dec<REG_OTHER>();  // idle warps of the producer / MMA warpgroup
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA of the pair leaves while the other may still touch its memory or TMEM
+  if (warp == WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+}  // namespace pair
+}  // namespace rw
+
+namespace rw {
+namespace pair {
+
+// Pairs that can be resident at once (cluster placement may leave SMs unused).
+int resident_pairs() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 74;
+  if (cached[dev] > 0) return cached[dev];
+  int n = 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (cudaFuncSetAttribute((const void*)attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, (const void*)attn_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    n = sms / 2;
+  }
+  cached[dev] = n;
+  return n;
+}
+
+int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, long long q_sb,
+           long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
+           long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
+           const rw_rope_t* rope, int* status, float* scratch, int nqp, int n_whole, int n_tail, int splits,
+           cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, mo;
+  if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, HD, q_sb, q_sl, q_sh, BM) ||
+      make_bf16_bl_hd_map(&mk, k, B, Lk, H, HD, k_sb, k_sl, k_sh, BN / 2) ||
+      make_bf16_bl_hd_map(&mv, v, B, Lk, H, HD, v_sb, v_sl, v_sh, BN) ||
+      make_bf16_bl_hd_map(&mo, o, B, Lq, H, HD, o_sb, o_sl, o_sh, BM))
+    return RW_ERR_DRIVER;
+  static unsigned long long attr_done = 0;
+  if (!ensure_smem_attr((const void*)attn_pair_kernel, SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
+  Params prm{};
+  prm.B = B;
+  prm.Lq = Lq;
+  prm.Lk = Lk;
+  prm.H = H;
+  prm.nqp = nqp;
+  prm.n_whole = n_whole;
+  prm.n_tail = n_tail;
+  prm.splits = splits;
+  prm.scale_log2 = scale_log2;
+  prm.status = status;
+  prm.scratch = scratch;
+  prm.rope_on = 0;
+  if (rope != nullptr) {
+    prm.rope = *rope;
+    prm.rope_on = 1;
+  }
+  const long long pairs = (long long)n_whole + (long long)n_tail * splits;
+  if (2 * pairs > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
+  attn_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}
+
+}  // namespace pair
+}  // namespace rw

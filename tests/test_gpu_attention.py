@@ -167,7 +167,7 @@ def test_attention_full_size_heads_vs_fp32_reference(cuda):
     _status_clean()
 
 
-@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 660, 2640, 24), (2, 300, 1000, 2)])
+@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 660, 2640, 40), (2, 300, 1000, 2)])
 def test_attention_key_split_matches_unsplit(cuda, B, Lq, Lk, H):
     """The key-split last wave (workspace given) and the whole-unit path (no
     workspace) compute the same attention."""
