@@ -127,7 +127,7 @@ def load_peaks():
 
 def profiled_traffic():
     """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "attn_fwd_ncu.txt")
+    p = os.path.join(ROOT, "profiles", "attn_pair_kernel_2640x34320.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):

@@ -33,11 +33,13 @@ constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
 
 // Merges the partial key ranges of each split unit: m = max m_p,
 // o = sum_p 2^((m_p - m) * scale_log2) * O_p / sum_p 2^((m_p - m) * scale_log2) * l_p.
-// One thread per query row; partial O is column-major so loads coalesce.
+// Block (unit, row half, column quarter); one thread per query row and 32 head
+// dims; partial O is column-major so the loads of a warp coalesce.
+constexpr int COMBINE_COLS = 32;
 __global__ void __launch_bounds__(128)
     combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
                    long long o_sh, int Lq, int H, int nqp, int n_whole, int splits, float scale_log2) {
-  const int e = blockIdx.x, i = blockIdx.y, r = threadIdx.x;
+  const int e = blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
   const int unit = n_whole + e;
   const int qp = unit % nqp, head = (unit / nqp) % H, b = unit / (nqp * H);
   const int row_tok = qp * 2 * BM + i * BM + r;
@@ -46,21 +48,22 @@ __global__ void __launch_bounds__(128)
   const float* slot0 = scratch + (size_t)e * splits * SLOT_FLOATS;
   float m = -INFINITY;
   for (int pc = 0; pc < splits; ++pc) m = fmaxf(m, slot0[pc * SLOT_FLOATS + 128 * 256 + row]);
-  float acc[128];
+  float acc[COMBINE_COLS];
 #pragma unroll
-  for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+  for (int c = 0; c < COMBINE_COLS; ++c) acc[c] = 0.f;
   float L = 0.f;
   for (int pc = 0; pc < splits; ++pc) {
     const float* sp = slot0 + pc * SLOT_FLOATS;
     const float w = exp2f((sp[128 * 256 + row] - m) * scale_log2);
     L += w * sp[128 * 256 + 256 + row];
 #pragma unroll
-    for (int c = 0; c < 128; ++c) acc[c] += w * sp[(size_t)c * 256 + row];
+    for (int c = 0; c < COMBINE_COLS; ++c) acc[c] += w * sp[(size_t)(c0 + c) * 256 + row];
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  uint4* dst = reinterpret_cast<uint4*>(out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh));
+  uint4* dst =
+      reinterpret_cast<uint4*>(out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh + c0));
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
+  for (int q = 0; q < COMBINE_COLS / 8; ++q) {
     uint4 v;
     v.x = pack_bf16x2(acc[8 * q + 0] * inv, acc[8 * q + 1] * inv);
     v.y = pack_bf16x2(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
@@ -151,7 +154,7 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
                               sc.splits, (cudaStream_t)stream);
   if (rc != RW_OK) return rc;
   if (sc.splits > 1) {
-    attn::combine_kernel<<<dim3(sc.n_tail, 2), 128, 0, (cudaStream_t)stream>>>(
+    attn::combine_kernel<<<dim3(sc.n_tail, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
         (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, sc.n_whole, sc.splits, scale_log2);
     if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
   }
