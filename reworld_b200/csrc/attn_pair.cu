@@ -360,13 +360,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             for (int e = 0; e < 32; ++e)
               if (64 * hh + 32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
         }
+        // eight independent 3-input max chains of depth 4, then a depth-3 tree
+        float a[8];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float a = fmax3(__uint_as_float(sr[c][0]), __uint_as_float(sr[c][1]), __uint_as_float(sr[c][2]));
-#pragma unroll
-          for (int e = 3; e + 1 < 32; e += 2) a = fmax3(a, __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-          row_max = fmax3(row_max, a, __uint_as_float(sr[c][31]));
+        for (int g = 0; g < 8; ++g) {
+          const uint32_t* v = &sr[g >> 2][(g & 3) * 8];
+          float t = fmax3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+          t = fmax3(t, __uint_as_float(v[3]), __uint_as_float(v[4]));
+          t = fmax3(t, __uint_as_float(v[5]), __uint_as_float(v[6]));
+          a[g] = fmaxf(t, __uint_as_float(v[7]));
         }
+        row_max = fmax3(row_max, fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]));
+        row_max = fmax3(row_max, a[6], a[7]);
       }
       // running maximum after key tile j - 1, from the warpgroup that handled it
       float m_prev = -INFINITY;
