@@ -216,6 +216,20 @@ int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, long long q_s
 int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P, int rank,
                       void* stream);
 
+/* rw_sp_attn_fwd: the attention of a sequence-parallel layer on this rank's heads
+ * with the head->seq exchange fused into its output: q [Lq, Hp, 128] (the whole
+ * chunk, this rank's Hp = H/P heads), k, v [Lk, Hp, 128] (this rank's cache
+ * view), element strides per token (sl) and head (sh).  Output row t, local head
+ * hl is written straight to out_ptrs[t / (Lq/P)] ([Lq/P, H, 128] bf16 per rank),
+ * row t % (Lq/P), head rank*Hp + hl, through peer pointers (DEVICE array of P
+ * pointers).  Same attention as rw_attn_fwd (workspace, rope, status alike);
+ * replaces the attention call of ulysses.py:44-52 together with the head->seq
+ * all_to_all of ulysses.py:54.  Cross-rank completion is the caller's barrier. */
+int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, int Hp, int D, long long q_sl,
+                   long long q_sh, long long k_sl, long long k_sh, long long v_sl, long long v_sh,
+                   const unsigned long long* out_ptrs, int P, int rank, int H, float softmax_scale,
+                   const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status, void* stream);
+
 /* Human-readable text of an RW_ERR_* code. */
 const char* rw_error_string(int code);
 

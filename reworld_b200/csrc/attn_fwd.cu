@@ -35,10 +35,14 @@ constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
 // o = sum_p 2^((m_p - m) * scale_log2) * O_p / sum_p 2^((m_p - m) * scale_log2) * l_p.
 // Block (unit, row half, column quarter); one thread per query row and 32 head
 // dims; partial O is column-major so the loads of a warp coalesce.
+// With peer_ptrs set (sequence-parallel layer, batch 1), row t of local head h
+// goes to rank t / peer_Ls, row t % peer_Ls, head peer_h0 + h of its [Ls, peer_H,
+// 128] buffer instead of `out`.
 constexpr int COMBINE_COLS = 32;
 __global__ void __launch_bounds__(128)
     combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
-                   long long o_sh, int Lq, int H, int nqp, int n_whole, int splits, float scale_log2) {
+                   long long o_sh, int Lq, int H, int nqp, int n_whole, int splits, float scale_log2,
+                   const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0) {
   const int e = blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
   const int unit = n_whole + e;
   const int qp = unit % nqp, head = (unit / nqp) % H, b = unit / (nqp * H);
@@ -60,8 +64,15 @@ __global__ void __launch_bounds__(128)
     for (int c = 0; c < COMBINE_COLS; ++c) acc[c] += w * sp[(size_t)(c0 + c) * 256 + row];
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  uint4* dst =
-      reinterpret_cast<uint4*>(out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh + c0));
+  uint8_t* row_base;
+  if (peer_ptrs != nullptr) {
+    const int owner = row_tok / peer_Ls;
+    row_base = reinterpret_cast<uint8_t*>(peer_ptrs[owner]) +
+               2 * (((long long)(row_tok - owner * peer_Ls) * peer_H + peer_h0 + head) * 128);
+  } else {
+    row_base = out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(row_base + 2 * c0);
 #pragma unroll
   for (int q = 0; q < COMBINE_COLS / 8; ++q) {
     uint4 v;
@@ -111,7 +122,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int n_whole, int n_tail, int splits,
-           cudaStream_t stream);
+           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream);
 }  // namespace pair
 }  // namespace rw
 
@@ -125,11 +136,18 @@ extern "C" long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H) {
   return (long long)sc.n_tail * sc.splits * attn::SLOT_FLOATS * (long long)sizeof(float);
 }
 
-extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H,
-                           int D, long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl,
-                           long long k_sh, long long v_sb, long long v_sl, long long v_sh, long long o_sb,
-                           long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope,
-                           void* workspace, long long workspace_bytes, int* status, void* stream) {
+namespace {
+
+struct PeerArgs {
+  const unsigned long long* ptrs;  // nullptr: output to o
+  int Ls, H, h0;
+};
+
+int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, int D, long long q_sb,
+             long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
+             long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float softmax_scale,
+             const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status, void* stream,
+             const PeerArgs& peer) {
   if (!q || !k || !v || !o) return RW_ERR_INVALID_ARG;
   if (D != attn::HD) return RW_ERR_UNSUPPORTED;
   if (B < 1 || Lq < 1 || Lk < 1 || H < 1 || B > 65535 || H > 65535) return RW_ERR_INVALID_ARG;
@@ -151,12 +169,38 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
   if (sc.splits > 1 && (workspace_bytes < need || !aligned16(workspace))) sc = attn::Schedule{units, 0, 1};
   const int rc = pair::launch(q, k, v, o, B, Lq, Lk, H, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb,
                               o_sl, o_sh, scale_log2, rope, status, (float*)workspace, nqp, sc.n_whole, sc.n_tail,
-                              sc.splits, (cudaStream_t)stream);
+                              sc.splits, peer.ptrs, peer.Ls, peer.H, peer.h0, (cudaStream_t)stream);
   if (rc != RW_OK) return rc;
   if (sc.splits > 1) {
     attn::combine_kernel<<<dim3(sc.n_tail, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
-        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, sc.n_whole, sc.splits, scale_log2);
+        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, sc.n_whole, sc.splits, scale_log2,
+        peer.ptrs, peer.Ls, peer.H, peer.h0);
     if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
   }
   return RW_OK;
+}
+
+}  // namespace
+
+extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H,
+                           int D, long long q_sb, long long q_sl, long long q_sh, long long k_sb, long long k_sl,
+                           long long k_sh, long long v_sb, long long v_sl, long long v_sh, long long o_sb,
+                           long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope,
+                           void* workspace, long long workspace_bytes, int* status, void* stream) {
+  return attn_run(q, k, v, o, B, Lq, Lk, H, D, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb, o_sl,
+                  o_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream, PeerArgs{nullptr, 0, 0, 0});
+}
+
+extern "C" int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, int Hp, int D,
+                              long long q_sl, long long q_sh, long long k_sl, long long k_sh, long long v_sl,
+                              long long v_sh, const unsigned long long* out_ptrs, int P, int rank, int H,
+                              float softmax_scale, const rw_rope_t* rope, void* workspace,
+                              long long workspace_bytes, int* status, void* stream) {
+  if (out_ptrs == nullptr || !q) return RW_ERR_INVALID_ARG;
+  if (P < 1 || rank < 0 || rank >= P || H < 1 || Hp < 1 || H != Hp * P || Lq < 1 || (Lq % P) != 0)
+    return RW_ERR_INVALID_ARG;
+  // o is never written in this mode; q's layout stands in for it in the unused output map
+  return attn_run(q, k, v, const_cast<void*>(q), 1, Lq, Lk, Hp, D, 0, q_sl, q_sh, 0, k_sl, k_sh, 0, v_sl, v_sh, 0,
+                  q_sl, q_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
+                  PeerArgs{out_ptrs, Lq / P, H, rank * Hp});
 }

@@ -64,6 +64,19 @@ constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 __host__ __device__ constexpr uint32_t tcol_o() { return 0u; }
 __host__ __device__ constexpr uint32_t tcol_s(int b) { return 128u + 128u * (uint32_t)b; }
 
+// Output of a sequence-parallel layer (batch 1): query token t, local head h goes
+// to rank t / Ls, row t % Ls, head h0 + h of that rank's [Ls, H, 128] bf16 buffer.
+struct PeerOut {
+  const unsigned long long* ptrs;  // device array: every rank's buffer base (peer pointers)
+  int Ls, H, h0;
+};
+
+__device__ __forceinline__ uint8_t* peer_row(const PeerOut& po, int t, int head) {
+  const int owner = t / po.Ls;
+  return reinterpret_cast<uint8_t*>(po.ptrs[owner]) +
+         2 * (((long long)(t - owner * po.Ls) * po.H + po.h0 + head) * 128);
+}
+
 // Work split, as in attn_fwd.cu but per pair: a unit is one (batch, head,
 // 256-row query block) over all keys; n_whole units run whole, the n_tail
 // remaining ones are cut into `splits` key ranges whose unnormalised partial
@@ -77,6 +90,7 @@ struct Params {
   rw_rope_t rope;
   int* status;
   float* scratch;
+  PeerOut peer;  // peer.ptrs == nullptr: output through tm_o (local); else rows go to their owner ranks
 };
 
 constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
@@ -497,6 +511,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         base[128 * 256 + row] = m_fin;
         base[128 * 256 + 256 + row] = l_row;
       }
+    } else if (ok && w < 2 && p.peer.ptrs != nullptr) {
+      // whole unit, sequence-parallel output: O / l -> bf16 stored straight into the
+      // owner rank's output row (head dims [64 w, 64 w + 64), 128 contiguous bytes)
+      tc_fence_after();
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      const int t = row0 + r;
+      uint8_t* dst = t < p.Lq ? peer_row(p.peer, t, head) + 128 * w : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 64 * w + 32 * c, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        if (dst != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + 16 * (c * 4 + q)) = v;
+          }
+        }
+      }
     } else if (ok && w < 2) {
       // whole unit: O / l -> bf16 -> shared memory (reusing the Q tile; every QK
       // completed before o_done) -> TMA store; warpgroup w writes box w
@@ -583,7 +622,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int n_whole, int n_tail, int splits,
-           cudaStream_t stream) {
+           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, mo;
   if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, HD, q_sb, q_sl, q_sh, BM) ||
       make_bf16_bl_hd_map(&mk, k, B, Lk, H, HD, k_sb, k_sl, k_sh, BN / 2) ||
@@ -604,6 +643,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   prm.scale_log2 = scale_log2;
   prm.status = status;
   prm.scratch = scratch;
+  prm.peer = PeerOut{peer_ptrs, peer_Ls, peer_H, peer_h0};
   prm.rope_on = 0;
   if (rope != nullptr) {
     prm.rope = *rope;

@@ -15,6 +15,7 @@ Exchange: one NCCL all_to_all_single over a contiguous buffer per tensor, with
 the layout transforms done by the package's kernels (rw_a2a_pack /
 rw_a2a_unpack) instead of chunk/contiguous/cat copies.
 """
+import math
 import torch
 import torch.distributed as dist
 
@@ -141,9 +142,9 @@ class UlyssesP2P:
 
     Per layer: rw_sp_scatter_qkv (each rank writes its sequence shard's q into
     the owning rank's q buffer and its roped k and v straight into the owning
-    rank's KV cache), a barrier, the chunk attention on the local heads over the
-    local (head-resident) cache, rw_sp_scatter_out (output rows back to the
-    ranks that own the tokens), a barrier.  The q buffer, output buffer and all
+    rank's KV cache), a barrier, rw_sp_attn_fwd (the chunk attention on the local
+    heads over the local, head-resident cache, whose epilogue stores every output
+    row straight into the buffer of the rank that owns the token), a barrier.  The q buffer, output buffer and all
     layers' caches are allocated as symmetric memory so every rank holds the
     peers' device pointers.  One sequence (B = 1), as in the streaming rollout.
     """
@@ -174,7 +175,6 @@ class UlyssesP2P:
         self.cache_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)   # [layer, k/v, P]
         self.q_ptrs = torch.tensor(list(self.h_q.buffer_ptrs), dtype=torch.int64, device=self.device)
         self.o_ptrs = torch.tensor(list(self.h_o.buffer_ptrs), dtype=torch.int64, device=self.device)
-        self.attn_out = torch.empty(1, chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
 
     def cache_k(self, layer):
         return self.caches[layer, 0].unsqueeze(0)
@@ -201,10 +201,30 @@ class UlyssesP2P:
                                      self.P, self.rank, _native.stream_ptr(self.device))
         _native.check(code, "rw_sp_scatter_out")
 
+    def attend(self, layer, lk, rope=None):
+        """Attention of this rank's heads over cache rows [0, lk) with the output
+        rows sent to their owner ranks' output buffers (complete after the next
+        barrier)."""
+        import ctypes
+        from .attention import _workspace
+        lib = _native.lib()
+        q = self.qbuf
+        kc, vc = self.caches[layer, 0], self.caches[layer, 1]
+        rs = rope.struct() if rope is not None else None
+        st = _native.status_tensor(self.device)
+        ws = _workspace(self.device, lib.rw_attn_workspace_bytes(1, self.L, lk, self.Hp))
+        code = lib.rw_sp_attn_fwd(
+            c_vp(q.data_ptr()), c_vp(kc.data_ptr()), c_vp(vc.data_ptr()), self.L, lk, self.Hp, self.D,
+            q.stride(0), q.stride(1), kc.stride(0), kc.stride(1), vc.stride(0), vc.stride(1),
+            c_vp(self.o_ptrs.data_ptr()), self.P, self.rank, self.H, 1.0 / math.sqrt(self.D),
+            ctypes.byref(rs) if rs is not None else None,
+            c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+            c_vp(st.data_ptr()), _native.stream_ptr(self.device))
+        _native.check(code, "rw_sp_attn_fwd")
+
     def layer(self, layer, q, k, v, dst_start, rope=None, attn_events=None):
         """One layer's cached chunk attention; returns [1, Ls, H, D] (this rank's
         tokens, all heads; valid until the next call's output exchange)."""
-        from .attention import chunk_attention
         for t in (q, k, v):
             if t.dtype != torch.bfloat16 or t.shape != (1, self.Ls, self.H, self.D) or t.stride(-1) != 1:
                 raise ValueError("q, k, v must be bf16 [1, L/P, H, D] with a contiguous head dim")
@@ -213,10 +233,8 @@ class UlyssesP2P:
         lk = dst_start + self.L
         if attn_events is not None:
             attn_events[0].record()
-        o = chunk_attention(self.qbuf.unsqueeze(0), self.cache_k(layer)[:, :lk], self.cache_v(layer)[:, :lk],
-                            rope=rope, out=self.attn_out)
+        self.attend(layer, lk, rope)
         if attn_events is not None:
             attn_events[1].record()
-        self.scatter_out(o[0])
         self.h_o.barrier(channel=0, timeout_ms=self.timeout_ms)
         return self.obuf.unsqueeze(0)
