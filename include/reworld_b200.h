@@ -35,6 +35,7 @@ extern "C" {
 #define RW_STATUS_TIMEOUT_SOFTMAX 0x04  /* softmax/epilogue wait ran out of time */
 #define RW_STATUS_TIMEOUT_COPY 0x08     /* bulk-copy wait ran out of time */
 #define RW_STATUS_BAD_SLOT 0x10         /* a descriptor/slot index was out of range */
+#define RW_STATUS_TIMEOUT_PEER 0x20     /* a cross-rank barrier wait ran out of time */
 
 /* 3-D RoPE parameters (the reference's causal_rope_apply + pm_rope_delta_apply).
  * freqs: the model's complex128 table [max_pos][64] stored as (real, imag)
@@ -215,6 +216,19 @@ int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, long long q_s
                       int P, int rank, int dst_start, int cap, const rw_rope_t* rope, void* stream);
 int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P, int rank,
                       void* stream);
+
+/* rw_sp_barrier: stream-ordered barrier of the P ranks of a sequence-parallel
+ * group over peer memory.  sig_ptrs: DEVICE array of P pointers to each rank's
+ * int32 signal array (symmetric, zero-initialised, at least slot_base + P
+ * entries).  Every rank calls it with the same slot_base and a strictly
+ * increasing epoch (> 0): rank r writes epoch into entry slot_base + r of every
+ * rank's array, after all its earlier work on the stream is visible to the
+ * peers, then waits (bounded: RW_STATUS_TIMEOUT_PEER in *status after
+ * timeout_ms) until its own entries slot_base .. slot_base + P - 1 hold epoch.
+ * Takes the place of the process-group barriers around the exchanges of
+ * wan_5b/distributed/ulysses.py:40-54. */
+int rw_sp_barrier(const unsigned long long* sig_ptrs, int slot_base, int P, int rank, int epoch, int timeout_ms,
+                  int* status, void* stream);
 
 /* rw_sp_attn_fwd: the attention of a sequence-parallel layer on this rank's heads
  * with the head->seq exchange fused into its output: q [Lq, Hp, 128] (the whole

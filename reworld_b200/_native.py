@@ -22,6 +22,7 @@ RW_STATUS_BITS = {
     0x04: "softmax/epilogue wait timed out",
     0x08: "bulk-copy wait timed out",
     0x10: "descriptor or slot index out of range",
+    0x20: "cross-rank barrier wait timed out",
 }
 
 
@@ -59,6 +60,7 @@ _SIGNATURES = {
     "rw_sp_scatter_qkv": (c_int, [c_vp, c_vp, c_vp] + [c_ll] * 6 + [c_vp, c_vp, c_vp] + [c_int] * 7
                           + [ctypes.POINTER(RwRope), c_vp]),
     "rw_sp_scatter_out": (c_int, [c_vp, c_vp] + [c_int] * 5 + [c_vp]),
+    "rw_sp_barrier": (c_int, [c_vp] + [c_int] * 5 + [c_vp, c_vp]),
     "rw_sp_attn_fwd": (c_int, [c_vp] * 3 + [c_int] * 4 + [c_ll] * 6 + [c_vp] + [c_int] * 3
                        + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
     "rw_error_string": (ctypes.c_char_p, [c_int]),

@@ -81,6 +81,37 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Cross-rank barrier: thread p signals rank p and waits for rank p's signal.
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(32) barrier_kernel(const unsigned long long* __restrict__ sig_ptrs, int slot_base,
+                                                     int P, int rank, int epoch, unsigned long long timeout_ns,
+                                                     int* status) {
+  const int p = threadIdx.x;
+  if (p < P) {
+    __threadfence_system();  // this rank's earlier stores (peer memory included) before the signal
+    st_release_sys(reinterpret_cast<int*>(sig_ptrs[p]) + slot_base + rank, epoch);
+    const int* mine = reinterpret_cast<const int*>(sig_ptrs[rank]) + slot_base + p;
+    if (ld_acquire_sys(mine) - epoch < 0) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(mine) - epoch < 0) {
+        if (globaltimer_ns() - t0 > timeout_ns) {
+          report_status(status, RW_STATUS_TIMEOUT_PEER);
+          break;
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
+
 inline unsigned grid_for(long long n) {
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
@@ -137,5 +168,15 @@ extern "C" int rw_sp_scatter_out(const void* o, const unsigned long long* out_ds
   if (!aligned16(o)) return RW_ERR_INVALID_ARG;
   sp::scatter_out_kernel<<<sp::grid_for((long long)L * (H / P) * 16), 256, 0, (cudaStream_t)stream>>>(
       (const uint8_t*)o, out_dst, L, H, H / P, P, rank);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}
+
+extern "C" int rw_sp_barrier(const unsigned long long* sig_ptrs, int slot_base, int P, int rank, int epoch,
+                             int timeout_ms, int* status, void* stream) {
+  if (!sig_ptrs) return RW_ERR_INVALID_ARG;
+  if (P < 1 || P > 32 || rank < 0 || rank >= P || slot_base < 0 || epoch <= 0 || timeout_ms <= 0)
+    return RW_ERR_INVALID_ARG;
+  sp::barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(sig_ptrs, slot_base, P, rank, epoch,
+                                                         (unsigned long long)timeout_ms * 1000000ull, status);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }

@@ -165,8 +165,14 @@ class UlyssesP2P:
         self.caches = symm.empty(n_layers, 2, cap_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
         self.qbuf = symm.empty(chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
         self.obuf = symm.empty(self.Ls, heads, head_dim, dtype=bf16, device=self.device)
+        self.sig = symm.empty(2 * self.P, dtype=torch.int32, device=self.device)   # barrier signal slots
         self.caches.zero_()
+        self.sig.zero_()
+        torch.cuda.synchronize(self.device)   # zeroed on every rank before any peer can signal into it
         self.h_c = symm.rendezvous(self.caches, group)
+        self.h_s = symm.rendezvous(self.sig, group)
+        self.sig_ptrs = torch.tensor(list(self.h_s.buffer_ptrs), dtype=torch.int64, device=self.device)
+        self.epoch = 0
         self.h_q = symm.rendezvous(self.qbuf, group)
         self.h_o = symm.rendezvous(self.obuf, group)
         per_tensor = cap_tokens * self.Hp * head_dim * 2
@@ -201,6 +207,16 @@ class UlyssesP2P:
                                      self.P, self.rank, _native.stream_ptr(self.device))
         _native.check(code, "rw_sp_scatter_out")
 
+    def barrier(self, slot_base):
+        """Stream-ordered barrier of the group over the peer-mapped signal array
+        (rw_sp_barrier); everything each rank enqueued before it is visible to all
+        ranks after it."""
+        lib = _native.lib()
+        st = _native.status_tensor(self.device)
+        code = lib.rw_sp_barrier(c_vp(self.sig_ptrs.data_ptr()), slot_base, self.P, self.rank, self.epoch,
+                                 self.timeout_ms, c_vp(st.data_ptr()), _native.stream_ptr(self.device))
+        _native.check(code, "rw_sp_barrier")
+
     def attend(self, layer, lk, rope=None):
         """Attention of this rank's heads over cache rows [0, lk) with the output
         rows sent to their owner ranks' output buffers (complete after the next
@@ -228,13 +244,14 @@ class UlyssesP2P:
         for t in (q, k, v):
             if t.dtype != torch.bfloat16 or t.shape != (1, self.Ls, self.H, self.D) or t.stride(-1) != 1:
                 raise ValueError("q, k, v must be bf16 [1, L/P, H, D] with a contiguous head dim")
+        self.epoch += 1
         self.scatter_qkv(layer, q, k, v, dst_start, rope)
-        self.h_q.barrier(channel=0, timeout_ms=self.timeout_ms)
+        self.barrier(0)
         lk = dst_start + self.L
         if attn_events is not None:
             attn_events[0].record()
         self.attend(layer, lk, rope)
         if attn_events is not None:
             attn_events[1].record()
-        self.h_o.barrier(channel=0, timeout_ms=self.timeout_ms)
+        self.barrier(self.P)
         return self.obuf.unsqueeze(0)

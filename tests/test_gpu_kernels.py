@@ -212,3 +212,29 @@ def test_a2a_pack_unpack_vs_oracle(cuda, P):
         got = a2a_unpack(blocks, H)
         assert np.array_equal(got.float().cpu().numpy(), back_want[r])
     _status_clean()
+
+
+def test_sp_barrier_single_rank_and_timeout(cuda):
+    """rw_sp_barrier completes at once for a group of one, and a wait for a peer
+    that never signals ends after its time limit with RW_STATUS_TIMEOUT_PEER in
+    the status word (no fault; the context stays usable)."""
+    import ctypes
+    from reworld_b200 import _native
+    lib = _native.lib()
+    stream = _native.stream_ptr(cuda)
+    sig = torch.zeros(2, 8, dtype=torch.int32, device=cuda)
+    ptrs = torch.tensor([sig[0].data_ptr(), sig[1].data_ptr()], dtype=torch.int64, device=cuda)
+    st = torch.zeros(4, dtype=torch.int32, device=cuda)
+    assert lib.rw_sp_barrier(ctypes.c_void_p(ptrs.data_ptr()), 0, 1, 0, 1, 1000,
+                             ctypes.c_void_p(st.data_ptr()), stream) == 0
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0 and int(sig[0, 0]) == 1
+    # two ranks on one device, rank 1 never signals: rank 0's wait runs out after 100 ms
+    assert lib.rw_sp_barrier(ctypes.c_void_p(ptrs.data_ptr()), 2, 2, 0, 5, 100,
+                             ctypes.c_void_p(st.data_ptr()), stream) == 0
+    torch.cuda.synchronize()
+    assert int(st[0]) & 0x20
+    assert int(sig[0, 2]) == 5 and int(sig[1, 2]) == 5     # rank 0 signalled both arrays
+    assert lib.rw_sp_barrier(ctypes.c_void_p(ptrs.data_ptr()), 0, 3, 5, 1, 100, None, stream) == -1   # rank >= P
+    x = torch.ones(16, device=cuda)
+    assert float((x * 2).sum()) == 32.0                      # context still usable
