@@ -11,12 +11,16 @@
 // causal_model.py:156-184 / action_model.py:40-51 is applied to q in shared
 // memory before the first QK^T, so raw (normed, un-roped) q can be passed.
 //
-// Work split.  A unit is one (batch, head, 256-row query block) over all keys,
-// run by one CTA pair.  When the units do not fill whole waves of resident
-// pairs, the first n_whole units run whole and each remaining unit is cut into
-// `splits` key ranges (pieces, ordered piece-major so that concurrently running
-// pairs share a head's K/V in L2); pieces write unnormalised partial results to
-// the caller's workspace and combine_kernel merges them.
+// Work split.  A unit is one (batch, head, 256-row query block) over all keys.
+// With a workspace, the resident CTA pairs (Np of them) run floor(U / Np) waves
+// of whole units (pair p: units p, p + Np, ...; the pairs busy at the same time
+// share heads, so K/V come from L2), then each walks an equal share of the
+// remaining units' key tiles, taken in unit-major order (a share may start and
+// end inside units).  The parts of units that a pair does not cover whole write
+// unnormalised partial results to two workspace slots per pair, which
+// combine_kernel merges.  Every pair thus gets the same work whatever the number
+// of units, and a unit is cut only where a share boundary falls.  Without a
+// workspace every pair runs one whole unit.
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
@@ -31,33 +35,48 @@ constexpr int HD = 128;  // head dim
 // one partial slot: O [128 columns][256 rows] fp32 (column-major), m [256], l [256]
 constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
 
-// Merges the partial key ranges of each split unit: m = max m_p,
-// o = sum_p 2^((m_p - m) * scale_log2) * O_p / sum_p 2^((m_p - m) * scale_log2) * l_p.
+// First tile of pair p's share of the T tiles (same arithmetic as the kernel).
+__host__ __device__ inline long long share_start(long long T, int Np, int p) { return T * p / Np; }
+
+// Merges the partial results of every tail unit that no single pair covered whole:
+// m = max m_s, o = sum_s 2^((m_s - m) * scale_log2) * O_s / sum_s 2^((m_s - m) * scale_log2) * l_s
+// over the unit's segments s.  The segment of pair p inside unit u sits in slot
+// 2p when it is p's first segment (p's share starts inside u), else in 2p + 1.
 // Block (unit, row half, column quarter); one thread per query row and 32 head
-// dims; partial O is column-major so the loads of a warp coalesce.
-// With peer_ptrs set (sequence-parallel layer, batch 1), row t of local head h
-// goes to rank t / peer_Ls, row t % peer_Ls, head peer_h0 + h of its [Ls, peer_H,
-// 128] buffer instead of `out`.
+// dims; partial O is column-major so the loads of a warp coalesce.  With
+// peer_ptrs set (sequence-parallel layer, batch 1), row t of local head h goes to
+// rank t / peer_Ls, row t % peer_Ls, head peer_h0 + h of its [Ls, peer_H, 128]
+// buffer instead of `out`.
 constexpr int COMBINE_COLS = 32;
 __global__ void __launch_bounds__(128)
     combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
-                   long long o_sh, int Lq, int H, int nqp, int n_whole, int splits, float scale_log2,
+                   long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
                    const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0) {
-  const int e = blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
-  const int unit = n_whole + e;
-  const int qp = unit % nqp, head = (unit / nqp) % H, b = unit / (nqp * H);
+  const int base = (U / Np) * Np;                  // units of the waves (written whole)
+  const int unit = base + (int)blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
+  const long long T = (long long)(U - base) * n_kv;
+  const long long a = (long long)(unit - base) * n_kv, b = a + n_kv;  // the unit's tail tiles [a, b)
+  auto pair_of = [&](long long t) {
+    int q = (int)(t * Np / T);
+    while (q + 1 < Np && share_start(T, Np, q + 1) <= t) ++q;
+    while (q > 0 && share_start(T, Np, q) > t) --q;
+    return q;
+  };
+  const int p_lo = pair_of(a), p_hi = pair_of(b - 1);
+  if (p_lo == p_hi && share_start(T, Np, p_lo) <= a && share_start(T, Np, p_lo + 1) >= b) return;  // written whole
+  const int qp = unit % nqp, head = (unit / nqp) % H, bb = unit / (nqp * H);  // global unit
   const int row_tok = qp * 2 * BM + i * BM + r;
   if (row_tok >= Lq) return;
   const int row = i * BM + r;
-  const float* slot0 = scratch + (size_t)e * splits * SLOT_FLOATS;
+  auto slot_of = [&](int q) { return share_start(T, Np, q) >= a ? 2 * q : 2 * q + 1; };
   float m = -INFINITY;
-  for (int pc = 0; pc < splits; ++pc) m = fmaxf(m, slot0[pc * SLOT_FLOATS + 128 * 256 + row]);
+  for (int q = p_lo; q <= p_hi; ++q) m = fmaxf(m, scratch[slot_of(q) * SLOT_FLOATS + 128 * 256 + row]);
   float acc[COMBINE_COLS];
 #pragma unroll
   for (int c = 0; c < COMBINE_COLS; ++c) acc[c] = 0.f;
   float L = 0.f;
-  for (int pc = 0; pc < splits; ++pc) {
-    const float* sp = slot0 + pc * SLOT_FLOATS;
+  for (int q = p_lo; q <= p_hi; ++q) {
+    const float* sp = scratch + (size_t)slot_of(q) * SLOT_FLOATS;
     const float w = exp2f((sp[128 * 256 + row] - m) * scale_log2);
     L += w * sp[128 * 256 + 256 + row];
 #pragma unroll
@@ -70,7 +89,7 @@ __global__ void __launch_bounds__(128)
     row_base = reinterpret_cast<uint8_t*>(peer_ptrs[owner]) +
                2 * (((long long)(row_tok - owner * peer_Ls) * peer_H + peer_h0 + head) * 128);
   } else {
-    row_base = out + 2 * ((long long)b * o_sb + (long long)row_tok * o_sl + head * o_sh);
+    row_base = out + 2 * ((long long)bb * o_sb + (long long)row_tok * o_sl + head * o_sh);
   }
   uint4* dst = reinterpret_cast<uint4*>(row_base + 2 * c0);
 #pragma unroll
@@ -84,34 +103,24 @@ __global__ void __launch_bounds__(128)
   }
 }
 
-// Chooses how many units run whole and into how many key ranges the rest is
-// cut: minimises (whole waves) + (waves of pieces) / splits + a per-wave cost of
-// ~1 % of a unit for each wave of pieces (pair start, Q load, pipeline ramp,
-// partial store); with no workspace, everything runs whole.  `slots` is the
-// number of units that run at once (resident CTA pairs).
-struct Schedule {
-  int n_whole, n_tail, splits;
+// Work shape of one call: Np pairs; `shared` when pairs share tail units
+// (workspace and merge needed; tail = the units after whole waves).
+struct Work {
+  int Np;
+  bool shared;
 };
 
-inline Schedule plan(int units, int n_kv, int slots, bool allow_split) {
-  Schedule best{units, 0, 1};
-  double best_cost = (double)((units + slots - 1) / slots);
-  if (!allow_split || slots <= 0) return best;
-  const int full_waves = units / slots;
-  for (int k = full_waves; k >= 0 && k >= full_waves - 1; --k) {
-    const int tail = units - k * slots;
-    if (tail <= 0) continue;
-    for (int S = 2; S <= 16 && S <= n_kv; ++S) {
-      const long long pieces = (long long)tail * S;
-      const long long waves = (pieces + slots - 1) / slots;
-      const double cost = k + (double)waves / S + 0.01 * (double)waves;
-      if (cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best = Schedule{k * slots, tail, S};
-      }
-    }
-  }
-  return best;
+inline Work work_for(int units, int n_kv, int resident, bool have_workspace) {
+  if (!have_workspace || resident < 1) return Work{units, false};
+  int Np = resident;
+  if ((long long)units * n_kv < Np) Np = units * n_kv;  // all of it is tail: one tile per pair at least
+  if (units % Np == 0) return Work{units, false};        // whole waves only
+  if ((long long)(units % Np) * n_kv < Np) return Work{units, false};  // tail too short to share
+  return Work{Np, true};
+}
+
+inline long long workspace_bytes_for(const Work& w) {
+  return w.shared ? 2LL * w.Np * SLOT_FLOATS * (long long)sizeof(float) : 0;
 }
 
 }  // namespace attn
@@ -121,7 +130,7 @@ int resident_pairs();
 int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, long long q_sb,
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
-           const rw_rope_t* rope, int* status, float* scratch, int nqp, int n_whole, int n_tail, int splits,
+           const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
            const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream);
 }  // namespace pair
 }  // namespace rw
@@ -132,8 +141,7 @@ extern "C" long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H) {
   if (B < 1 || Lq < 1 || Lk < 1 || H < 1) return 0;
   const int nqp = (Lq + 2 * attn::BM - 1) / (2 * attn::BM);
   const int n_kv = (Lk + attn::BN - 1) / attn::BN;
-  const attn::Schedule sc = attn::plan(B * H * nqp, n_kv, pair::resident_pairs(), true);
-  return (long long)sc.n_tail * sc.splits * attn::SLOT_FLOATS * (long long)sizeof(float);
+  return attn::workspace_bytes_for(attn::work_for(B * H * nqp, n_kv, pair::resident_pairs(), true));
 }
 
 namespace {
@@ -164,16 +172,17 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
   const int nqp = (Lq + 2 * attn::BM - 1) / (2 * attn::BM);
   const int n_kv = (Lk + attn::BN - 1) / attn::BN;
   const int units = B * H * nqp;
-  attn::Schedule sc = attn::plan(units, n_kv, pair::resident_pairs(), workspace != nullptr);
-  const long long need = (long long)sc.n_tail * sc.splits * attn::SLOT_FLOATS * (long long)sizeof(float);
-  if (sc.splits > 1 && (workspace_bytes < need || !aligned16(workspace))) sc = attn::Schedule{units, 0, 1};
+  attn::Work wk = attn::work_for(units, n_kv, pair::resident_pairs(), workspace != nullptr);
+  if (wk.shared && (workspace_bytes < attn::workspace_bytes_for(wk) || !aligned16(workspace)))
+    wk = attn::work_for(units, n_kv, 0, false);
   const int rc = pair::launch(q, k, v, o, B, Lq, Lk, H, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb,
-                              o_sl, o_sh, scale_log2, rope, status, (float*)workspace, nqp, sc.n_whole, sc.n_tail,
-                              sc.splits, peer.ptrs, peer.Ls, peer.H, peer.h0, (cudaStream_t)stream);
+                              o_sl, o_sh, scale_log2, rope, status, wk.shared ? (float*)workspace : nullptr, nqp,
+                              units, wk.Np, peer.ptrs, peer.Ls, peer.H, peer.h0, (cudaStream_t)stream);
   if (rc != RW_OK) return rc;
-  if (sc.splits > 1) {
-    attn::combine_kernel<<<dim3(sc.n_tail, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
-        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, sc.n_whole, sc.splits, scale_log2,
+  if (wk.shared) {
+    const int tail_units = units - (units / wk.Np) * wk.Np;
+    attn::combine_kernel<<<dim3(tail_units, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
+        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, units, wk.Np, scale_log2,
         peer.ptrs, peer.Ls, peer.H, peer.h0);
     if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
   }

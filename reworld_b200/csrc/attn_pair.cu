@@ -77,14 +77,22 @@ __device__ __forceinline__ uint8_t* peer_row(const PeerOut& po, int t, int head)
          2 * (((long long)(t - owner * po.Ls) * po.H + po.h0 + head) * 128);
 }
 
-// Work split, as in attn_fwd.cu but per pair: a unit is one (batch, head,
-// 256-row query block) over all keys; n_whole units run whole, the n_tail
-// remaining ones are cut into `splits` key ranges whose unnormalised partial
-// results (O, m, l; fp32) go to the scratch slots merged by combine_kernel (attn_fwd.cu).
+// Work.  A unit is one (batch, head, 256-row query block) over all key tiles.
+// Of the U units, the first W = floor(U / Np) * Np run whole in waves: pair p of
+// the Np pairs runs units p, p + Np, ..., so the pairs working at the same time
+// share heads and their K/V tiles come from L2.  The key tiles of the remaining
+// units form one sequence of T = (U - W) x n_kv tiles (unit-major); pair p then
+// walks the tiles [p T / Np, (p + 1) T / Np) as segments (the parts of its range
+// inside one unit).  A segment covering a whole unit writes the output; any
+// other one writes its unnormalised partial result (O, m, l; fp32) to scratch
+// slot 2p (the pair's first tail segment) or 2p + 1 (its last), merged by
+// combine_kernel (attn_fwd.cu).  With Np = U every pair runs one whole unit and
+// no scratch is used.
 struct Params {
   int B, Lq, Lk, H;
   int nqp;
-  int n_whole, n_tail, splits;
+  int U;        // units
+  int Np;       // pairs in the grid
   float scale_log2;
   int rope_on;
   rw_rope_t rope;
@@ -92,8 +100,6 @@ struct Params {
   float* scratch;
   PeerOut peer;  // peer.ptrs == nullptr: output through tm_o (local); else rows go to their owner ranks
 };
-
-constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
 
 struct __align__(8) Barriers {
   uint64_t pre_full;             // even CTA: both CTAs' K halves of key tiles 0-2 landed
@@ -116,6 +122,66 @@ struct Ctx {
   uint32_t peer_abort;  // shared::cluster address of the peer's abort flag
   int* status;
 };
+
+constexpr long long SLOT_FLOATS = 128LL * 256 + 2 * 256;
+
+struct Seg {
+  int unit, kv0, kv1, slot;  // slot -1: whole unit (output written directly)
+};
+
+// Segments of one pair, in order: its whole units of the waves, then the parts
+// of its tail range.
+struct SegIter {
+  long long t, t0, t1;  // tail range, in tiles after the waves' units
+  int n_kv, pair, Np, w, waves, base;
+  __device__ __forceinline__ SegIter(const Params& p, int pair_, int n_kv_)
+      : n_kv(n_kv_), pair(pair_), Np(p.Np), w(0) {
+    waves = p.U / p.Np;
+    base = waves * p.Np;
+    const long long T = (long long)(p.U - base) * n_kv_;
+    t0 = T * pair_ / p.Np;
+    t1 = T * (pair_ + 1) / p.Np;
+    t = t0;
+  }
+  __device__ __forceinline__ bool next(Seg& sg) {
+    if (w < waves) {
+      sg.unit = w * Np + pair;
+      sg.kv0 = 0;
+      sg.kv1 = n_kv;
+      sg.slot = -1;
+      ++w;
+      return true;
+    }
+    if (t >= t1) return false;
+    const long long u = t / n_kv;
+    const long long ue = (u + 1) * n_kv;
+    const long long e = t1 < ue ? t1 : ue;
+    sg.unit = base + (int)u;
+    sg.kv0 = (int)(t - u * n_kv);
+    sg.kv1 = (int)(e - u * n_kv);
+    sg.slot = (sg.kv0 == 0 && sg.kv1 == n_kv) ? -1 : (t == t0 ? 2 * pair : 2 * pair + 1);
+    t = e;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void init_barriers(Barriers& sb) {
+  mbar_init(&sb.pre_full, 1);
+  for (int t = 0; t < NSTAGE; ++t) {
+    mbar_init(&sb.stage_full[t], 1);
+    mbar_init(&sb.stage_free[t], 1);
+  }
+  mbar_init(&sb.q_full, 1);
+  mbar_init(&sb.q_ready, 2 * 256);
+  for (int b = 0; b < NSBUF; ++b) {
+    mbar_init(&sb.s_full[b], 1);
+    mbar_init(&sb.p_ready[b], 2 * BM);
+  }
+  for (int b = 0; b < NSBUF; ++b) mbar_init(&sb.m_ready[b], BM);
+  mbar_init(&sb.o_done, 1);
+  mbar_init(&sb.epi, 256);
+  mbar_init(&sb.drain, 1);
+}
 
 // Bounded wait; on expiry raises this CTA's and the peer's abort flags and
 // records `err` in the status word.
@@ -173,41 +239,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int n_kv_all = (p.Lk + BN - 1) / BN;
   const int kv_tail = p.Lk - (n_kv_all - 1) * BN;
   const int pair_id = blockIdx.x >> 1;
-  int unit, kv0, kv1, slot = -1;
-  if (pair_id < p.n_whole) {
-    unit = pair_id;
-    kv0 = 0;
-    kv1 = n_kv_all;
-  } else {
-    const int t = pair_id - p.n_whole;
-    const int e = t % p.n_tail, piece = t / p.n_tail;
-    unit = p.n_whole + e;
-    kv0 = (int)((long long)piece * n_kv_all / p.splits);
-    kv1 = (int)((long long)(piece + 1) * n_kv_all / p.splits);
-    slot = e * p.splits + piece;
-  }
-  const int qp = unit % p.nqp;
-  const int head = (unit / p.nqp) % p.H;
-  const int bidx = unit / (p.nqp * p.H);
-  const int row0 = qp * (2 * BM) + (int)rank * BM;  // this CTA's first query row
-  const int n_kv = kv1 - kv0;
 
   if (threadIdx.x == WARP_LOAD * 32) {
-    mbar_init(&sb.pre_full, 1);
-    for (int t = 0; t < NSTAGE; ++t) {
-      mbar_init(&sb.stage_full[t], 1);
-      mbar_init(&sb.stage_free[t], 1);
-    }
-    mbar_init(&sb.q_full, 1);
-    mbar_init(&sb.q_ready, 2 * 256);
-    for (int b = 0; b < NSBUF; ++b) {
-      mbar_init(&sb.s_full[b], 1);
-      mbar_init(&sb.p_ready[b], 2 * BM);
-    }
-    for (int b = 0; b < NSBUF; ++b) mbar_init(&sb.m_ready[b], BM);
-    mbar_init(&sb.o_done, 1);
-    mbar_init(&sb.epi, 256);
-    mbar_init(&sb.drain, 1);
+    init_barriers(sb);
     sb.abort_flag = 0;
     fence_mbar_init();
   }
@@ -221,6 +255,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
   const Ctx cx{&sb, mapa_shared(smem_u32(&sb.abort_flag), rank ^ 1u), p.status};
+  // Between two segments, every thread of both CTAs: all work of the segment is
+  // done (the producer drained its barriers, the MMA issuer its MMAs, the
+  // epilogue its store) before either CTA starts the next one.  The barriers
+  // keep running: a per-key-tile barrier is indexed by the pair's running key
+  // tile count J (buffer J mod 3, stage J mod NSTAGE, phase parity from J), a
+  // once-per-segment barrier by the parity of the segment index.
+  auto boundary = [&]() {
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+  };
+  auto aborted = [&]() { return *(volatile int*)&sb.abort_flag != 0; };
+  // per-segment coordinates, same in every role
+  struct SegPos {
+    int kv0, n_kv, slot, head, bidx, row0;
+  };
+  auto seg_pos = [&](const Seg& sg) {
+    SegPos q;
+    q.kv0 = sg.kv0;
+    q.n_kv = sg.kv1 - sg.kv0;
+    q.slot = sg.slot;
+    const int qp = sg.unit % p.nqp;
+    q.head = (sg.unit / p.nqp) % p.H;
+    q.bidx = sg.unit / (p.nqp * p.H);
+    q.row0 = qp * (2 * BM) + (int)rank * BM;  // this CTA's first query row
+    return q;
+  };
 
   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -230,6 +291,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_o);
+    }
+    SegIter it(p, pair_id, n_kv_all);
+    Seg sg;
+    int J0 = 0, segi = 0;  // key tiles and segments of this pair before the current one
+    for (bool first = true; it.next(sg); first = false, J0 += sg.kv1 - sg.kv0, ++segi) {
+    if (!first) boundary();
+    const uint32_t sph = (uint32_t)segi & 1u;  // phase parity of the once-per-segment barriers
+    const SegPos sp = seg_pos(sg);
+    const int kv0 = sp.kv0, n_kv = sp.n_kv, head = sp.head, bidx = sp.bidx, row0 = sp.row0;
+    if (lane == 0 && !aborted()) {
       const uint64_t pol = l2_policy_evict_last();  // K/V tiles are re-read by the other query pairs of the head
       mbar_expect_tx(&sb.q_full, Q_BYTES);
       tma_load_4d(smem_q, &tm_q, &sb.q_full, 0, head, row0, bidx);
@@ -246,8 +317,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const uint32_t pre_bar = mapa_shared(smem_u32(&sb.pre_full), 0);
       for (int kt = 0; kt < n_pre; ++kt) load_k(pre + kt * HALF_TILE, pre_bar, kt);
       for (int j = 0; j < n_kv; ++j) {
-        const int t = j % NSTAGE;
-        if (j >= NSTAGE && !(ok = pwait(&sb.stage_free[t], (uint32_t)(j / NSTAGE - 1) & 1u, cx, RW_STATUS_TIMEOUT_LOAD)))
+        const int J = J0 + j;
+        const int t = J % NSTAGE;
+        if (J >= NSTAGE && !(ok = pwait(&sb.stage_free[t], (uint32_t)(J / NSTAGE - 1) & 1u, cx, RW_STATUS_TIMEOUT_LOAD)))
           break;
         const bool has_k = j + NSBUF < n_kv;
         if (even) mbar_expect_tx(&sb.stage_full[t], 2 * HALF_TILE * (has_k ? 2 : 1));
@@ -257,19 +329,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (has_k) load_k(st + HALF_TILE, bar, j + NSBUF);
       }
       // The even CTA sees every issued copy of the pair complete on its barriers
-      // (already consumed by the MMA issuer on the normal path).
+      // (already consumed by the MMA issuer on the normal path); both CTAs see the
+      // last stage releases land (multicast commits nobody else waits for), so
+      // no arrival is in flight when the barriers are set up for the next segment.
+      const int last = n_kv > NSTAGE ? n_kv - NSTAGE : 0;
       if (even) {
-        mbar_wait_drain(&sb.pre_full, 0);
-        const int first = n_kv > NSTAGE ? n_kv - NSTAGE : 0;
-        for (int j = first; j < n_kv; ++j) mbar_wait_drain(&sb.stage_full[j % NSTAGE], (uint32_t)(j / NSTAGE) & 1u);
+        mbar_wait_drain(&sb.pre_full, sph);
+        for (int J = J0 + last; J < J0 + n_kv; ++J)
+          mbar_wait_drain(&sb.stage_full[J % NSTAGE], (uint32_t)(J / NSTAGE) & 1u);
       }
-      mbar_wait_drain(&sb.q_full, 0);
+      if (ok)
+        for (int J = J0 + last; J < J0 + n_kv; ++J)
+          mbar_wait_drain(&sb.stage_free[J % NSTAGE], (uint32_t)(J / NSTAGE) & 1u);
+      mbar_wait_drain(&sb.q_full, sph);
     }
     __syncwarp();
+    }
   } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
     setmaxnreg_dec<REG_OTHER>();
-    if (even) {
+    SegIter it(p, pair_id, n_kv_all);
+    Seg sg;
+    int J0 = 0, segi = 0;  // key tiles and segments of this pair before the current one
+    for (bool first = true; it.next(sg); first = false, J0 += sg.kv1 - sg.kv0, ++segi) {
+    if (!first) boundary();
+    const uint32_t sph = (uint32_t)segi & 1u;  // phase parity of the once-per-segment barriers
+    const int n_kv = sg.kv1 - sg.kv0;
+    if (even && !aborted()) {
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(2 * BM, BN, 0, 0);  // Q K-major, K K-major
       constexpr uint32_t IDESC_PV = idesc_bf16_f32(2 * BM, HD, 0, 1);  // P from TMEM, V MN-major
       // Descriptor bases; a byte offset d within a buffer is added as d >> 4 (the
@@ -296,23 +382,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // twice (S of tile j + 3 ready, stage j free): waits and commits cost ~100
       // clocks each and an MMA issue ~50, so one thread keeps up with 1024
       // clocks of tensor work per key tile only with this little bookkeeping.
-      bool ok = pwait_warp(&sb.q_ready, 0, cx, RW_STATUS_TIMEOUT_MMA) &&
-                pwait_warp(&sb.pre_full, 0, cx, RW_STATUS_TIMEOUT_MMA);
+      bool ok = pwait_warp(&sb.q_ready, sph, cx, RW_STATUS_TIMEOUT_MMA) &&
+                pwait_warp(&sb.pre_full, sph, cx, RW_STATUS_TIMEOUT_MMA);
       tc_fence_after();
       if (ok) {
         const int n_pre = n_kv < NSBUF ? n_kv : NSBUF;
         if (elect_one()) {
           for (int kt = 0; kt < n_pre; ++kt) {
-            issue_qk(tmem + tcol_s(kt), dq, dk_pre + kt * PRE_DESC);
-            tc_commit_pair_mc(&sb.s_full[kt], 0x3);
+            const int bk = (J0 + kt) % NSBUF;
+            issue_qk(tmem + tcol_s(bk), dq, dk_pre + kt * PRE_DESC);
+            tc_commit_pair_mc(&sb.s_full[bk], 0x3);
           }
         }
         __syncwarp();
       }
-      int b = 0, t = 0;
+      int b = J0 % NSBUF, t = J0 % NSTAGE;
       for (int j = 0; j < n_kv && ok; ++j) {
-        if (!(ok = pwait_warp(&sb.p_ready[b], (uint32_t)(j / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
-        if (!(ok = pwait_warp(&sb.stage_full[t], (uint32_t)(j / NSTAGE) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
+        const int J = J0 + j;
+        if (!(ok = pwait_warp(&sb.p_ready[b], (uint32_t)(J / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
+        if (!(ok = pwait_warp(&sb.stage_full[t], (uint32_t)(J / NSTAGE) & 1u, cx, RW_STATUS_TIMEOUT_MMA))) break;
         tc_fence_after();
         if (elect_one()) {
           issue_pv(tmem + tcol_o(), tmem + tcol_s(b), dv_st + t * STAGE_DESC, j > 0);
@@ -330,9 +418,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (elect_one()) {
         tc_commit_pair_mc(&sb.drain, 0x1);
-        mbar_wait_drain(&sb.drain, 0);
+        mbar_wait_drain(&sb.drain, sph);
       }
       __syncwarp();
+    }
     }
   } else if (warp < 4 * NWG) {
     // ------------------------------------------------------------ softmax + epilogue (both CTAs)
@@ -343,7 +432,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tO = tmem + lane_base + tcol_o();
     const float sl2 = p.scale_log2;
     const uint32_t p_ready_cl0 = mapa_shared(smem_u32(&sb.p_ready[0]), 0);
-    bool ok = pwait_warp(&sb.q_full, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX);
+    SegIter it(p, pair_id, n_kv_all);
+    Seg sg;
+    int n_epi = 0;  // whole units stored through shared memory so far (completions of `epi`)
+    int J0 = 0, segi = 0;  // key tiles and segments of this pair before the current one
+    for (bool first = true; it.next(sg); first = false, J0 += sg.kv1 - sg.kv0, ++segi) {
+    if (!first) boundary();
+    const uint32_t sph = (uint32_t)segi & 1u;  // phase parity of the once-per-segment barriers
+    const SegPos sp = seg_pos(sg);
+    const int kv0 = sp.kv0, n_kv = sp.n_kv, slot = sp.slot, head = sp.head, bidx = sp.bidx, row0 = sp.row0;
+    bool ok = !aborted() && pwait_warp(&sb.q_full, sph, cx, RW_STATUS_TIMEOUT_SOFTMAX);
     if (ok && w < 2) {
       if (p.rope_on) rope_row_half(smem_q, r, w, row0 + r, bidx, p.rope);
       fence_proxy_async_smem();
@@ -352,9 +450,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     float m_base = -INFINITY;  // exponent base of this warpgroup's partial row sum
     uint64_t l2 = 0ull;        // packed (even-column, odd-column) partial row sums
     for (int j = w; j < n_kv && ok; j += NWG) {
-      const int b = j % NSBUF;  // S buffer of key tile j
+      const int J = J0 + j;
+      const int b = J % NSBUF;  // S buffer of key tile j
       const uint32_t tS = tmem + lane_base + tcol_s(b);
-      if (!(ok = pwait_warp(&sb.s_full[b], (uint32_t)(j / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX))) break;
+      if (!(ok = pwait_warp(&sb.s_full[b], (uint32_t)(J / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX))) break;
       tc_fence_after();
       const bool tail = kv0 + j == n_kv_all - 1 && kv_tail < BN;
       // pass 1: row maximum, 64 columns at a time (registers are kept for pass 2)
@@ -390,10 +489,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // running maximum after key tile j - 1, from the warpgroup that handled it
       float m_prev = -INFINITY;
       if (j > 0) {
-        const int jp = j - 1;
-        if (!(ok = pwait_warp(&sb.m_ready[jp % NSBUF], (uint32_t)(jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
+        const int Jp = J - 1;
+        if (!(ok = pwait_warp(&sb.m_ready[Jp % NSBUF], (uint32_t)(Jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
           break;
-        m_prev = m_sh[jp % NSBUF][r];
+        m_prev = m_sh[Jp % NSBUF][r];
       }
       const float m_new = fmaxf(m_prev, row_max);
       const bool need = (m_new - m_prev) * sl2 > RESCALE_THRESHOLD;
@@ -405,7 +504,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // (PV(j) is issued only after this warpgroup publishes P(j)).
         const float alpha = need ? fast_exp2((m_prev - m_use) * sl2) : 1.f;
         // stage_free of key tile j - 1 is committed after PV(j-1)
-        if (!(ok = pwait_warp(&sb.stage_free[(j - 1) % NSTAGE], (uint32_t)((j - 1) / NSTAGE) & 1u, cx,
+        if (!(ok = pwait_warp(&sb.stage_free[(J - 1) % NSTAGE], (uint32_t)((J - 1) / NSTAGE) & 1u, cx,
                               RW_STATUS_TIMEOUT_SOFTMAX)))
           break;
         tc_fence_after();
@@ -491,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (lg > 0.f) l_row += lg * fast_exp2((fin[2 * g][r] - m_fin) * sl2);
     }
     ok = __all_sync(0xffffffffu, ok) && !*(volatile int*)&sb.abort_flag;
-    if (ok && w < 2) ok = pwait_warp(&sb.o_done, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX);
+    if (ok && w < 2) ok = pwait_warp(&sb.o_done, sph, cx, RW_STATUS_TIMEOUT_SOFTMAX);
     if (ok && w < 2 && slot >= 0) {
       // partial key range: unnormalised O columns [64 w, 64 w + 64) (column-major),
       // the exponent base and the row sum, for combine_kernel
@@ -561,7 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&sb.epi);
       if (threadIdx.x == 0) {
-        if (pwait(&sb.epi, 0, cx, RW_STATUS_TIMEOUT_SOFTMAX)) {
+        if (pwait(&sb.epi, (uint32_t)n_epi & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)) {
           tma_store_4d(&tm_o, smem_q, 0, head, row0, bidx);
           tma_store_4d(&tm_o, smem_q + Q_HALF, 64, head, row0, bidx);
           bulk_commit_group();
@@ -569,10 +668,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    if (slot < 0 && p.peer.ptrs == nullptr) ++n_epi;
+    }
   } else {
     setmaxnreg_dec<REG_OTHER>();  // idle warps of the producer / MMA warpgroup
+    SegIter it(p, pair_id, n_kv_all);
+    Seg sg;
+    for (bool first = true; it.next(sg); first = false)
+      if (!first) boundary();
   }
 
+  if (warp == WARP_LOAD && lane == 0 && aborted()) {
+    // After a timeout some copies may have been issued without the matching
+    // wait (the odd CTA's copies complete on the even CTA's barriers): give them
+    // time to land before either CTA leaves.
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 200000ull) {
+    }
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA of the pair leaves while the other may still touch its memory or TMEM
@@ -621,7 +734,7 @@ int resident_pairs() {
 int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, long long q_sb,
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
-           const rw_rope_t* rope, int* status, float* scratch, int nqp, int n_whole, int n_tail, int splits,
+           const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
            const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, mo;
   if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, HD, q_sb, q_sl, q_sh, BM) ||
@@ -637,9 +750,8 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   prm.Lk = Lk;
   prm.H = H;
   prm.nqp = nqp;
-  prm.n_whole = n_whole;
-  prm.n_tail = n_tail;
-  prm.splits = splits;
+  prm.U = U;
+  prm.Np = Np;
   prm.scale_log2 = scale_log2;
   prm.status = status;
   prm.scratch = scratch;
@@ -649,9 +761,9 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
     prm.rope = *rope;
     prm.rope_on = 1;
   }
-  const long long pairs = (long long)n_whole + (long long)n_tail * splits;
-  if (2 * pairs > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
-  attn_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+  if (Np < 1 || U < 1 || 2LL * Np > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
+  if (U % Np != 0 && (long long)(U % Np) * ((Lk + BN - 1) / BN) < Np) return RW_ERR_INVALID_ARG;  // empty tail shares
+  attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
 

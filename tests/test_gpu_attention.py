@@ -167,10 +167,12 @@ def test_attention_full_size_heads_vs_fp32_reference(cuda):
     _status_clean()
 
 
-@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 660, 2640, 40), (2, 300, 1000, 2)])
+@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 2640, 34320, 6), (1, 2640, 34320, 3),
+                                         (1, 660, 2640, 40), (2, 300, 1000, 2)])
 def test_attention_key_split_matches_unsplit(cuda, B, Lq, Lk, H):
-    """The key-split last wave (workspace given) and the whole-unit path (no
-    workspace) compute the same attention."""
+    """Pairs sharing units (workspace given: equal shares of the key tiles, partial
+    results merged) and one whole unit per pair (no workspace) compute the same
+    attention; 3 and 6 heads are the per-rank shapes at 8 and 4 GPUs."""
     import ctypes
     from reworld_b200 import _native, chunk_attention
     g = torch.Generator(device=cuda).manual_seed(Lq + Lk)
