@@ -447,7 +447,75 @@ def gpu_side_baselines(ro, dev):
     nbytes = 2 * 2 * N_LAYERS * (N_SINK + RECENT_W + len(R)) * CT * ro.H * HEAD_DIM * 2   # read + write, k + v
     out["gather_ms"] = round(msg, 3)
     out["gather_gbs"] = round(nbytes / (msg * 1e-3) / 1e9, 1)
+    out["qkv_norm_rope_store"] = qkv_norm_measure(ro, dev, timeit)
     return out
+
+
+def _torch_rms(x, w, eps=1e-6):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)).type_as(x) * w
+
+
+def qkv_norm_measure(ro, dev, timeit, n_rot=4):
+    """The step before the attention for one layer's chunk (2640 tokens x 3072):
+    q/k RMSNorm + RoPE of k + cache write of k and v, as one rw_qkv_norm_rope_store
+    launch, against the unfused path it replaces on the same inputs (torch's two
+    WanRMSNorm evaluations + rw_rope_kv_store).  The launches rotate over n_rot
+    layers' inputs and caches (n_rot x 48.7 MB of q|k|v rows, more than L2)."""
+    from reworld_b200 import qkv_norm_rope_store, rope_kv_store
+    C = HEADS * HEAD_DIM
+    g = torch.Generator(device=dev).manual_seed(77)
+    qkv = [(torch.randn(1, CT, 3 * C, generator=g, device=dev) * 1.5).to(torch.bfloat16) for _ in range(n_rot)]
+    wq = (1 + 0.05 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    wk = (1 + 0.05 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    qo = [torch.empty(1, CT, HEADS, HEAD_DIM, dtype=torch.bfloat16, device=dev) for _ in range(n_rot)]
+    rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), 0)
+    it = [0]
+
+    def fused():
+        i = it[0] % n_rot
+        it[0] += 1
+        x = qkv[i]
+        qkv_norm_rope_store(x[..., :C], x[..., C:2 * C], x[..., 2 * C:], wq, wk, ro.cache_k[i], ro.cache_v[i],
+                            ro.tot, 1e-6, rope=rope, q_out=qo[i])
+
+    def unfused():
+        i = it[0] % n_rot
+        it[0] += 1
+        x = qkv[i]
+        _torch_rms(x[..., :C], wq)
+        k = _torch_rms(x[..., C:2 * C], wk).view(1, CT, HEADS, HEAD_DIM)
+        rope_kv_store(k, x[..., 2 * C:].view(1, CT, HEADS, HEAD_DIM), ro.cache_k[i], ro.cache_v[i], ro.tot,
+                      rope=rope)
+
+    def graph_of(fn):
+        # the n_rot calls captured once: replays time the GPU work, not the Python around it
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(n_rot):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        it[0] = 0
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(n_rot):
+                fn()
+        return gr
+
+    g_f, g_u = graph_of(fused), graph_of(unfused)
+    ms_f = timeit(g_f.replay, n=8) / n_rot
+    ms_u = timeit(g_u.replay, n=8) / n_rot
+    nbytes = CT * C * 2 * 6 + 2 * C * 2          # q, k, v rows in; q, k, v rows out; two weight vectors
+    _, _, hbm, peak_src = load_peaks()
+    gbs = nbytes / (ms_f * 1e-3) / 1e9
+    return {"ms": round(ms_f, 4), "gbs": round(gbs, 1), "bytes_per_launch": nbytes,
+            "frac_of_hbm": round(gbs / hbm, 4), "hbm_peak_gbs": hbm, "peak_kind": f"copy bandwidth ({peak_src})",
+            "unfused_ms": round(ms_u, 4), "speedup_vs_unfused": round(ms_u / ms_f, 2),
+            "shape": f"1 x {CT} tokens x {C} (24 heads x 128), RoPE on k, cache write at row {ro.tot}",
+            "unfused": "torch WanRMSNorm formula on q and k (GPU) + rw_rope_kv_store",
+            "timing": f"CUDA graph of {n_rot} launches over {n_rot} layers' inputs and caches, replayed; "
+                      "per launch"}
 
 
 # ------------------------------------------------------------------ CPU baseline / reference arm

@@ -114,6 +114,28 @@ int rw_rope_kv_store(const void* k, const void* v, const void* q_in, void* q_out
                      long long ck_sl, long long ck_sh, long long cv_sb, long long cv_sl, long long cv_sh,
                      const rw_rope_t* rope, void* stream);
 
+/* RMSNorm of the new chunk's q and k projections over all heads, RoPE(+PM-RoPE)
+ * of k, and the cache write of k and v, in one launch:
+ *   q_out[b, t]               = rmsnorm(q_in[b, t]) * w_q
+ *   cache_k[b, dst_start + t] = rope(rmsnorm(k_in[b, t]) * w_k)
+ *   cache_v[b, dst_start + t] = v_in[b, t]
+ * Replaces wan_5b/modules/action_model.py:164-166 (norm_q / norm_k, WanRMSNorm of
+ * wan_5b/modules/model.py:73-89) with the k half of :265-292.  q_in, k_in, v_in
+ * are bf16 [B, L, H*D] rows (element strides *_sb, *_sl; channels contiguous),
+ * w_q / w_k bf16 [H*D]; q_out [B, L, H, D] and the caches [B, cap, H, D] take
+ * strides as in rw_attn_fwd.  q is returned without RoPE (the attention applies
+ * it).  eps_q / eps_k are the two norms' epsilons.  rope may be NULL.  D must be
+ * 128 and H <= 288 (one token's three rows, 6*H*D bytes, fit a 216 KB stage).
+ * The rows are staged through shared memory by bulk copies whose waits are
+ * bounded: a wait that runs out of time sets RW_STATUS_TIMEOUT_COPY in *status
+ * (optional). */
+int rw_qkv_norm_rope_store(const void* q_in, const void* k_in, const void* v_in, const void* w_q, const void* w_k,
+                           void* q_out, void* cache_k, void* cache_v, int B, int L, int H, int D, int dst_start,
+                           float eps_q, float eps_k, long long qi_sb, long long qi_sl, long long ki_sb,
+                           long long ki_sl, long long vi_sb, long long vi_sl, long long qo_sb, long long qo_sl,
+                           long long qo_sh, long long ck_sb, long long ck_sl, long long ck_sh, long long cv_sb,
+                           long long cv_sl, long long cv_sh, const rw_rope_t* rope, int* status, void* stream);
+
 /* One byte-copy job of the landmark/cache assembly: nbytes from src to dst,
  * both 16-byte aligned, nbytes a multiple of 16. */
 typedef struct rw_copy_desc {

@@ -68,11 +68,17 @@ def causal_rope_apply(x, grid_sizes, freqs, start_frame=0):
 def pm_rope_delta_apply(x, delta):
     """action_model.py:40-51.  x: [B, L, n, d] bf16 values; delta: [B, L, 1, d/2]
     fp32 phases.  cos/sin come from torch.polar in fp32 like the reference."""
+    cr, ci = delta_cos_sin(delta)
+    return pm_rope_apply_cs(x, cr, ci)
+
+
+def pm_rope_apply_cs(x, cr, ci):
+    """pm_rope_delta_apply with the phase factor given as its fp32 (cos, sin)
+    parts [B, L, 1, d/2] (e.g. the factor torch.polar formed on the GPU, where
+    the reference runs it)."""
     x = np.asarray(x, dtype=np.float32)
-    dt = torch.as_tensor(np.asarray(delta, dtype=np.float32))
-    rot = torch.polar(torch.ones_like(dt), dt)
-    cr = rot.real.numpy().astype(np.float32)
-    ci = rot.imag.numpy().astype(np.float32)
+    cr = np.asarray(cr, dtype=np.float32)
+    ci = np.asarray(ci, dtype=np.float32)
     B, L, n, d = x.shape
     xc = x.reshape(B, L, n, d // 2, 2)
     ar, ai = xc[..., 0], xc[..., 1]

@@ -19,7 +19,9 @@ from .numerics import bits_to_torch_bf16, f32_to_bf16_bits
 from .rope import causal_rope_apply, pm_rope_delta_apply
 
 
-def _rms(x, w, eps):
+def rms_norm(x, w, eps):
+    """WanRMSNorm.forward (wan_5b/modules/model.py:82-89): fp32 mean of squares,
+    rsqrt, .type_as(x), times the weight."""
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
     return y.type_as(x) * w
@@ -66,8 +68,8 @@ def prop_self_attn_forward(W, x, grid, freqs, kv_cache, current_start, prope_con
     b, s = x.shape[:2]
     n = num_heads
     d = x.shape[-1] // n
-    q = _rms(_lin(x, W["q.weight"], W["q.bias"]), W["norm_q.weight"], eps).view(b, s, n, d)
-    k = _rms(_lin(x, W["k.weight"], W["k.bias"]), W["norm_k.weight"], eps).view(b, s, n, d)
+    q = rms_norm(_lin(x, W["q.weight"], W["q.bias"]), W["norm_q.weight"], eps).view(b, s, n, d)
+    k = rms_norm(_lin(x, W["k.weight"], W["k.bias"]), W["norm_k.weight"], eps).view(b, s, n, d)
     v = _lin(x, W["v.weight"], W["v.bias"]).view(b, s, n, d)
     f, h, w = grid
     fs = h * w

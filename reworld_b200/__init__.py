@@ -15,8 +15,8 @@ from . import _native
 _native.lib()   # fail loudly at import when the CUDA library is absent
 
 from .attention import attention, chunk_attention, flash_attention  # noqa: E402
-from .kv_cache import rope_kv_store  # noqa: E402
+from .kv_cache import qkv_norm_rope_store, rope_kv_store  # noqa: E402
 from .rope import RopeArgs, build_freqs, device_table, rope_params  # noqa: E402
 
-__all__ = ["attention", "flash_attention", "chunk_attention", "rope_kv_store", "RopeArgs", "build_freqs",
-           "rope_params", "device_table"]
+__all__ = ["attention", "flash_attention", "chunk_attention", "rope_kv_store", "qkv_norm_rope_store", "RopeArgs",
+           "build_freqs", "rope_params", "device_table"]

@@ -43,23 +43,32 @@ __device__ __forceinline__ RopeToken rope_token(const rw_rope_t& rp, int token, 
   return rt;
 }
 
-// Rotates one packed bf16 pair (low half = real, high half = imaginary) that is
-// complex pair j of the token.
-__device__ __forceinline__ uint32_t rope_pair(uint32_t w, int j, const RopeToken& rt) {
-  const double2 cs = (j < rt.e_t) ? rt.ft[j] : ((j < rt.e_h) ? rt.fh[j] : rt.fw[j]);
+// The freqs entry of complex pair j of the token.
+__device__ __forceinline__ double2 rope_freq(int j, const RopeToken& rt) {
+  return (j < rt.e_t) ? rt.ft[j] : ((j < rt.e_h) ? rt.fh[j] : rt.fw[j]);
+}
+
+// Rotates one packed bf16 pair (low half = real, high half = imaginary) by the
+// freqs entry cs, then, when has_d, by the PM-RoPE factor d = (cos, sin).
+__device__ __forceinline__ uint32_t rope_rotate(uint32_t w, double2 cs, bool has_d, float2 d) {
   const double xr = (double)bf16_lo(w);
   const double xi = (double)bf16_hi(w);
   const double yr = __dsub_rn(__dmul_rn(xr, cs.x), __dmul_rn(xi, cs.y));
   const double yi = __dadd_rn(__dmul_rn(xr, cs.y), __dmul_rn(xi, cs.x));
   uint32_t o = pack_bf16x2(__double2float_rn(yr), __double2float_rn(yi));
-  if (rt.dl != nullptr) {
-    const float2 d = rt.dl[j];
+  if (has_d) {
     const float ar = bf16_lo(o), ai = bf16_hi(o);
     const float zr = __fsub_rn(__fmul_rn(ar, d.x), __fmul_rn(ai, d.y));
     const float zi = __fadd_rn(__fmul_rn(ar, d.y), __fmul_rn(ai, d.x));
     o = pack_bf16x2(zr, zi);
   }
   return o;
+}
+
+// Rotates one packed bf16 pair that is complex pair j of the token.
+__device__ __forceinline__ uint32_t rope_pair(uint32_t w, int j, const RopeToken& rt) {
+  const bool has_d = rt.dl != nullptr;
+  return rope_rotate(w, rope_freq(j, rt), has_d, has_d ? rt.dl[j] : make_float2(0.f, 0.f));
 }
 
 // Rotates 4 consecutive pairs (one 16-byte chunk: elements 8*c16 .. 8*c16+7).

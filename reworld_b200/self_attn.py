@@ -9,9 +9,11 @@ P^-1 residual when prope_context is given, the chunk's RoPE at its start frame
 [local_end - num_new, local_end), attention over kv_cache[:, :local_end], the
 index updates of :304-305 and the o projection (+ P residual).
 
-What runs on the B200 kernels: the RoPE of k and the cache write of k/v (one
-rw_rope_kv_store launch) and the attention with q's RoPE applied inside the
-kernel (rw_attn_fwd).  The projections, RMSNorm and the PRoPE residual
+What runs on the B200 kernels: for a bf16 module, the RMSNorm of q and k, the
+RoPE of k and the cache write of k/v (one rw_qkv_norm_rope_store launch; a
+module in another dtype keeps torch's norm and uses rw_rope_kv_store), and the
+attention with q's RoPE applied inside the kernel (rw_attn_fwd).  The q/k/v
+projections run as one cuBLAS GEMM over the stacked weights; the PRoPE residual
 matmuls stay torch GPU ops.  The KV cache must be bf16.
 
 Install it per block the way the reference installs its sequence-parallel
@@ -23,7 +25,7 @@ import types
 import torch
 
 from .attention import chunk_attention
-from .kv_cache import rope_kv_store
+from .kv_cache import qkv_norm_rope_store, rope_kv_store
 from .rope import RopeArgs, device_table
 
 
@@ -52,6 +54,37 @@ def se3_block_apply(x, prope_context, mode, frame_seqlen):
     return y.reshape(B, H, L, D).permute(0, 2, 1, 3)
 
 
+def _stacked_qkv(self):
+    """The q/k/v projections' weights [3C, C] (and biases [3C]) in one buffer, so
+    that one GEMM computes all three.  The module's own parameters are re-pointed
+    to views of that buffer the first time (the values are unchanged and no
+    second copy is kept); if they are later replaced, the buffer is rebuilt."""
+    lins = (self.q, self.k, self.v)
+    W = getattr(self, "_rw_wqkv", None)
+    C = lins[0].weight.shape[0]
+    if W is None or any(m.weight.data_ptr() != W[i * C].data_ptr() for i, m in enumerate(lins)):
+        W = torch.cat([m.weight.detach() for m in lins])
+        for i, m in enumerate(lins):
+            m.weight.data = W[i * C:(i + 1) * C]
+        self._rw_wqkv = W
+    if all(m.bias is not None for m in lins):
+        bias = getattr(self, "_rw_bqkv", None)
+        if bias is None or any(m.bias.data_ptr() != bias[i * C].data_ptr() for i, m in enumerate(lins)):
+            bias = torch.cat([m.bias.detach() for m in lins])
+            for i, m in enumerate(lins):
+                m.bias.data = bias[i * C:(i + 1) * C]
+            self._rw_bqkv = bias
+    else:
+        bias = torch.cat([m.bias.detach() if m.bias is not None else W.new_zeros(C) for m in lins])
+    return W, bias
+
+
+def _fused_path(self, x):
+    return x.dtype == torch.bfloat16 and all(
+        t.dtype == torch.bfloat16 for t in (self.q.weight, self.k.weight, self.v.weight, self.norm_q.weight,
+                                            self.norm_k.weight))
+
+
 def _cache_local_size(local_attn_size):
     if isinstance(local_attn_size, (list, tuple)):
         finite = [abs(sz) for sz in local_attn_size if sz != -1]
@@ -69,9 +102,16 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
     if kv_cache["k"].dtype != torch.bfloat16:
         raise NotImplementedError("the B200 chunk-attention path keeps the KV cache in bf16")
     b, s, n, d = *x.shape[:2], self.num_heads, self.head_dim
-    q = self.norm_q(self.q(x)).view(b, s, n, d)
-    k = self.norm_k(self.k(x)).view(b, s, n, d)
-    v = self.v(x).view(b, s, n, d)
+    fused = _fused_path(self, x)
+    if fused:
+        C = n * d
+        qkv = torch.nn.functional.linear(x, *_stacked_qkv(self))        # [b, s, 3C]
+        q_rows, k_rows, v_rows = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+        v = v_rows.view(b, s, n, d)
+    else:
+        q = self.norm_q(self.q(x)).view(b, s, n, d)
+        k = self.norm_k(self.k(x)).view(b, s, n, d)
+        v = self.v(x).view(b, s, n, d)
     g0 = [int(t) for t in grid_sizes[0].tolist()]
     frame_seqlen = g0[1] * g0[2]
 
@@ -84,8 +124,10 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         delta = self.pose_mlp(c_all[:, -T_half:])                  # [B, T, d/2] per-frame phase
         v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen)
         v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
+        if fused:
+            v_rows = v.flatten(2)
 
-    num_new = q.shape[1]
+    num_new = s
     cur_end = current_start + num_new
     sink_tokens = self.sink_size * frame_seqlen
     cache_local = _cache_local_size(self.local_attn_size)
@@ -112,7 +154,11 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
 
     table = device_table(freqs, x.device)
     rope = RopeArgs(table, grid, g_start_f, head_dim=d, delta=delta)
-    rope_kv_store(k, v, kv_cache["k"], kv_cache["v"], local_start, rope=rope)
+    if fused:
+        q = qkv_norm_rope_store(q_rows, k_rows, v_rows, self.norm_q.weight, self.norm_k.weight, kv_cache["k"],
+                                kv_cache["v"], local_start, self.norm_q.eps, self.norm_k.eps, rope=rope)
+    else:
+        rope_kv_store(k, v, kv_cache["k"], kv_cache["v"], local_start, rope=rope)
     if self.max_attention_size is None:
         k_slice = kv_cache["k"][:, :local_end]
         v_slice = kv_cache["v"][:, :local_end]

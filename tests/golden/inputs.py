@@ -25,6 +25,26 @@ def checksum(*tensors):
     return h
 
 
+RMSNORM_DIM, RMSNORM_EPS = 3072, 1e-6      # the 5B model's width (24 heads x 128) and its norms' eps
+
+
+def rmsnorm_case():
+    """bf16 rows [2, 12, 3072] for the q/k RMSNorm: Gaussian rows with per-row
+    scales from 1e-3 to 1e2, one all-zero row and one row holding a single large
+    entry; norm weights ~ 1 + N(0, 0.05) rounded to bf16 (one for q, one for k)."""
+    g = torch.Generator().manual_seed(23)
+    B, L, C = 2, 12, RMSNORM_DIM
+    scale = torch.logspace(-3, 2, B * L).reshape(B, L, 1)
+    x = torch.randn(B, L, C, generator=g) * scale
+    x[0, 5] = 0.0
+    x[1, 7] = 0.0
+    x[1, 7, 100] = 50.0
+    x = x.to(torch.bfloat16)
+    wq = (1.0 + torch.randn(C, generator=g) * 0.05).to(torch.bfloat16)
+    wk = (1.0 + torch.randn(C, generator=g) * 0.05).to(torch.bfloat16)
+    return x, wq, wk
+
+
 def attention_case(i):
     B, Lq, Lk, H = ATTN_CASES[i]
     g = torch.Generator().manual_seed(100 + i)

@@ -19,6 +19,7 @@ tests); each fixture keeps a checksum of its inputs and the reference's outputs:
                     with and without prope_context: output, new cache rows
   landmark.npz      LandmarkCacheV2 runs: retrieved index lists, bank contents,
                     events and write_into_cache bytes of the last chunks
+  rmsnorm.npz       WanRMSNorm (the q/k norms) on bf16 rows of the 5B width
   ulysses.npz       wan_5b/distributed/util.all_to_all (seq->head and back)
                     over gloo process groups of 2 and 4 ranks (gloo lacks
                     all_to_all; it is emulated by its definition with all_gather)
@@ -96,6 +97,20 @@ def gen_rope():
     yd = pm_rope_delta_apply(causal_rope_apply(x, grid, freqs, start_frame=7).type_as(x), delta)
     np.savez_compressed(os.path.join(HERE, "rope.npz"), freqs_head=torch.view_as_real(freqs[:48]).numpy(),
                         checksum=np.array(gi.checksum(x, delta)), rope_delta_sf7=bits(yd), **outs)
+
+
+def gen_rmsnorm():
+    from wan_5b.modules.model import WanRMSNorm
+    x, wq, wk = gi.rmsnorm_case()
+    out = {"checksum": np.array(gi.checksum(x, wq, wk))}
+    for tag, w in (("q", wq), ("k", wk)):
+        norm = WanRMSNorm(gi.RMSNORM_DIM, eps=gi.RMSNORM_EPS)
+        with torch.no_grad():
+            norm.weight.copy_(w.float())
+        norm = norm.to(torch.bfloat16)
+        with torch.no_grad():
+            out[f"norm_{tag}"] = bits(norm(x))
+    np.savez_compressed(os.path.join(HERE, "rmsnorm.npz"), **out)
 
 
 def gen_self_attn(att):
@@ -226,11 +241,13 @@ def main():
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     att = setup_reference(a.reference)
-    todo = a.only.split(",") if a.only else ["attention", "rope", "self_attn", "landmark", "ulysses"]
+    todo = a.only.split(",") if a.only else ["attention", "rope", "rmsnorm", "self_attn", "landmark", "ulysses"]
     if "attention" in todo:
         gen_attention(att)
     if "rope" in todo:
         gen_rope()
+    if "rmsnorm" in todo:
+        gen_rmsnorm()
     if "self_attn" in todo:
         gen_self_attn(att)
     if "landmark" in todo:

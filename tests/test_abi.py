@@ -69,6 +69,18 @@ def test_other_entry_points_reject_bad_arguments():
     z = [0] * 18
     assert lib.rw_rope_kv_store(p, p, None, None, p, p, 1, 8, 2, 64, 0, *z, None, None) == -2
     assert lib.rw_rope_kv_store(p, p, p, None, p, p, 1, 8, 2, 128, 0, *z, None, None) == -1
+    # rw_qkv_norm_rope_store: every rejection happens before a launch
+    s15 = [3 * 256, 3 * 256] * 3 + [256, 256, 128] * 3
+    ok8 = [p] * 8
+    fn = lib.rw_qkv_norm_rope_store
+    assert fn(*ok8, 1, 0, 2, 128, 0, 1e-6, 1e-6, *s15, None, None, None) == 0             # L = 0: nothing to do
+    assert fn(*([None] + ok8[1:]), 1, 8, 2, 128, 0, 1e-6, 1e-6, *s15, None, None, None) == -1   # null pointer
+    assert fn(*ok8, 1, 8, 2, 64, 0, 1e-6, 1e-6, *s15, None, None, None) == -2             # head_dim 64
+    assert fn(*ok8, 1, 8, 289, 128, 0, 1e-6, 1e-6, *s15, None, None, None) == -2          # 6*H*D > 216 KB
+    assert fn(*ok8, 1, 8, 2, 128, 0, -1.0, 1e-6, *s15, None, None, None) == -1            # eps < 0
+    assert fn(*ok8, 1, 8, 2, 128, -1, 1e-6, 1e-6, *s15, None, None, None) == -1           # dst_start < 0
+    assert fn(*([ctypes.c_void_p(18)] + ok8[1:]), 1, 8, 2, 128, 0, 1e-6, 1e-6, *s15, None, None, None) == -1
+    assert fn(*ok8, 1, 8, 2, 128, 0, 1e-6, 1e-6, *(s15[:1] + [12] + s15[2:]), None, None, None) == -1  # row stride % 8
 
 
 def test_import_fails_loudly_without_library(monkeypatch, tmp_path):

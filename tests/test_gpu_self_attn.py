@@ -69,6 +69,10 @@ def test_forward_matches_reference_fixture(cuda, golden, tag, dtype, with_ctx):
         y = mod.forward(x.to(cuda), torch.tensor([ct]), torch.tensor([[f, h, w]]), freqs, None, kv_cache=cache,
                         current_start=n0, prope_context=ctx.to(cuda) if ctx is not None else None)
     torch.cuda.synchronize()
+    # the bf16 module ran the stacked q|k|v GEMM and the fused norm/RoPE/store kernel;
+    # its parameters are views of the stacked buffer and keep their values
+    assert mod.q.weight.data_ptr() == mod._rw_wqkv.data_ptr()
+    assert torch.equal(mod.v.weight.cpu(), vals["v.weight"].to(dtype))
     # cache bookkeeping exactly as the reference
     assert [int(cache["global_end_index"]), int(cache["local_end_index"])] == list(g[f"{tag}_ends"])
     assert torch.equal(cache["k"][:, :n0].cpu(), k0) and not cache["k"][:, n0 + ct:].any()

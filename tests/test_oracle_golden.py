@@ -35,6 +35,18 @@ def test_attention_oracle_matches_reference(golden, i):
     assert err.max() < 1e-2 and err.mean() < 1e-3
 
 
+@pytest.mark.parametrize("tag", ["q", "k"])
+def test_rmsnorm_oracle_matches_reference(golden, tag):
+    """The oracle's WanRMSNorm restatement reproduces the reference's bf16 bits
+    (zero row, tiny and large rows included)."""
+    g = golden["rmsnorm"]
+    x, wq, wk = gi.rmsnorm_case()
+    assert abs(gi.checksum(x, wq, wk) - float(g["checksum"])) < 1e-6, "input generator drifted"
+    y = osa.rms_norm(x, wq if tag == "q" else wk, gi.RMSNORM_EPS)
+    assert y.dtype == torch.bfloat16
+    assert np.array_equal(torch_bf16_to_bits(y), g[f"norm_{tag}"].reshape(x.shape))
+
+
 def test_rope_table_matches_reference(golden):
     g = golden["rope"]
     fr = orope.build_freqs(128, gi.ROPE_SCALE_H, gi.ROPE_SCALE_W)
