@@ -448,7 +448,45 @@ def gpu_side_baselines(ro, dev):
     out["gather_ms"] = round(msg, 3)
     out["gather_gbs"] = round(nbytes / (msg * 1e-3) / 1e9, 1)
     out["qkv_norm_rope_store"] = qkv_norm_measure(ro, dev, timeit)
+    out["se3_block_apply"] = se3_measure(ro, dev, timeit)
     return out
+
+
+def _graph(dev, fn, n):
+    """fn() called n times, captured once (after one uncaptured round on a side stream)."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(n):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for i in range(n):
+            fn(i)
+    return gr
+
+
+def se3_measure(ro, dev, timeit, n_rot=8):
+    """The PRoPE SE3 transform of one layer's chunk activations [1, 2640, 24, 128]
+    (rw_se3_block_apply) against the reference's torch formulation of
+    _se3_block_apply on the same inputs; launches rotate over n_rot layers'
+    activations (n_rot x 16.2 MB, more than L2), timed from CUDA-graph replays."""
+    from reworld_b200.self_attn import _se3_torch, se3_block_apply
+    ctx = torch.eye(4, device=dev).repeat(1, 5, 1, 1)
+    ctx[..., :3, 3] = torch.tensor([0.3, -0.2, 1.1], device=dev)
+    outs = [torch.empty_like(ro.q[i]) for i in range(n_rot)]
+    g_k = _graph(dev, lambda i: se3_block_apply(ro.q[i], ctx, "P", TOK_H * TOK_W, out=outs[i]), n_rot)
+    g_t = _graph(dev, lambda i: _se3_torch(ro.q[i], ctx, "P", TOK_H * TOK_W), n_rot)
+    ms_k = timeit(g_k.replay, n=8) / n_rot
+    ms_t = timeit(g_t.replay, n=8) / n_rot
+    nbytes = 2 * CT * HEADS * HEAD_DIM * 2
+    _, _, hbm, peak_src = load_peaks()
+    gbs = nbytes / (ms_k * 1e-3) / 1e9
+    return {"ms": round(ms_k, 4), "gbs": round(gbs, 1), "bytes_per_launch": nbytes,
+            "frac_of_hbm": round(gbs / hbm, 4), "peak_kind": f"copy bandwidth ({peak_src})",
+            "torch_ms": round(ms_t, 4), "speedup_vs_torch": round(ms_t / ms_k, 2),
+            "shape": f"1 x {CT} tokens x 24 heads x 128, 3 frames", "timing": "CUDA graph replay, per launch"}
 
 
 def _torch_rms(x, w, eps=1e-6):

@@ -136,6 +136,18 @@ int rw_qkv_norm_rope_store(const void* q_in, const void* k_in, const void* v_in,
                            long long qo_sh, long long ck_sb, long long ck_sl, long long ck_sh, long long cv_sb,
                            long long cv_sl, long long cv_sh, const rw_rope_t* rope, int* status, void* stream);
 
+/* PRoPE SE3 transform: out[b, t, h, 4g+i] = sum_k M[b, t / frame_seqlen][i][k] * x[b, t, h, 4g+k]
+ * for every group of 4 head-dim channels.  Replaces _se3_block_apply
+ * (wan_5b/modules/action_model.py:84-114) as used for the V-side P^-1 residual
+ * (:194-203) and the O-side P residual (:307-318).  mats: fp32 [B, L/frame_seqlen,
+ * 4, 4] in device memory holding the frames' matrices in the activation dtype's
+ * values (P, or P^-1 inverted as the reference inverts it), 16-byte aligned.
+ * x, out: bf16 [B, L, H, D] with element strides; L a multiple of frame_seqlen;
+ * D must be 128.  fp32 accumulation, one rounding to bf16 per output. */
+int rw_se3_block_apply(const void* x, void* out, const float* mats, int B, int L, int H, int D, int frame_seqlen,
+                       long long x_sb, long long x_sl, long long x_sh, long long o_sb, long long o_sl,
+                       long long o_sh, void* stream);
+
 /* One byte-copy job of the landmark/cache assembly: nbytes from src to dst,
  * both 16-byte aligned, nbytes a multiple of 16. */
 typedef struct rw_copy_desc {

@@ -24,6 +24,8 @@ import types
 
 import torch
 
+from . import _native
+from ._native import c_vp
 from .attention import chunk_attention
 from .kv_cache import qkv_norm_rope_store, rope_kv_store
 from .rope import RopeArgs, device_table
@@ -41,17 +43,37 @@ def _invert_se3(T):
     return out
 
 
-def se3_block_apply(x, prope_context, mode, frame_seqlen):
-    """Block-diagonal 4x4 transform over head_dim per frame (action_model.py:84-114,
-    with its optional translation bound off as by default).  x: [B, L, H, D]."""
-    B, L, H, D = x.shape
-    nf = L // frame_seqlen
-    ctx = prope_context[:, -nf:].to(x.dtype)
+def se3_mats(prope_context, mode, n_frames, dtype):
+    """The frames' 4x4 matrices as _se3_block_apply forms them (action_model.py:
+    96-104, translation bound off as by default): the last n_frames contexts cast
+    to the activation dtype, inverted in that dtype for 'P_inv'; returned as fp32
+    [B, n_frames, 4, 4] (same values) for the kernel."""
+    ctx = prope_context[:, -n_frames:].to(dtype)
     if mode == "P_inv":
         ctx = _invert_se3(ctx)
-    xv = x.permute(0, 2, 1, 3).reshape(B, H, nf, frame_seqlen, D // 4, 4)
-    y = torch.matmul(ctx[:, None, :, None, None], xv.unsqueeze(-1)).squeeze(-1)
-    return y.reshape(B, H, L, D).permute(0, 2, 1, 3)
+    return ctx.float().contiguous()
+
+
+def se3_block_apply(x, prope_context, mode, frame_seqlen, out=None):
+    """Block-diagonal 4x4 transform over head_dim per frame (action_model.py:84-114)
+    with one rw_se3_block_apply launch.  x: bf16 [B, L, H, 128] on the GPU (any
+    strides with a contiguous head dim); returns `out` (default: a new contiguous
+    [B, L, H, 128] tensor)."""
+    B, L, H, D = x.shape
+    if x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError("se3_block_apply runs on bf16 CUDA tensors")
+    if L % frame_seqlen != 0:
+        raise ValueError(f"{L} tokens are not whole frames of {frame_seqlen}")
+    mats = se3_mats(prope_context, mode, L // frame_seqlen, x.dtype).to(x.device)
+    if out is None:
+        out = torch.empty((B, L, H, D), dtype=torch.bfloat16, device=x.device)
+    lib = _native.lib()
+    with torch.cuda.device(x.device):
+        code = lib.rw_se3_block_apply(c_vp(x.data_ptr()), c_vp(out.data_ptr()), c_vp(mats.data_ptr()), B, L, H, D,
+                                      int(frame_seqlen), *x.stride()[:3], *out.stride()[:3],
+                                      _native.stream_ptr(x.device))
+    _native.check(code, "rw_se3_block_apply")
+    return out
 
 
 def _stacked_qkv(self):
@@ -79,10 +101,41 @@ def _stacked_qkv(self):
     return W, bias
 
 
+def _stacked_out(self):
+    """[W_o | W_prope] as one [C, 2C] weight (the module's o / prope_proj weights
+    re-pointed to its column blocks, values unchanged) and b_o + b_prope, so that
+    o(y) + prope_proj(P y) is one GEMM over [y | P y]."""
+    W = getattr(self, "_rw_wout", None)
+    C = self.o.weight.shape[0]
+    if W is None or self.o.weight.data_ptr() != W.data_ptr() or \
+            self.prope_proj.weight.data_ptr() != W[:, C:].data_ptr():
+        W = torch.cat([self.o.weight.detach(), self.prope_proj.weight.detach()], dim=1)
+        self.o.weight.data = W[:, :C]
+        self.prope_proj.weight.data = W[:, C:]
+        self._rw_wout = W
+    bo, bp = self.o.bias, self.prope_proj.bias
+    if bo is None and bp is None:
+        return W, None
+    bias = (bo.detach() if bo is not None else 0) + (bp.detach() if bp is not None else 0)
+    return W, bias
+
+
 def _fused_path(self, x):
     return x.dtype == torch.bfloat16 and all(
         t.dtype == torch.bfloat16 for t in (self.q.weight, self.k.weight, self.v.weight, self.norm_q.weight,
                                             self.norm_k.weight))
+
+
+def _se3_torch(x, prope_context, mode, frame_seqlen):
+    """The transform with torch ops, for modules outside the bf16 kernels' domain."""
+    B, L, H, D = x.shape
+    nf = L // frame_seqlen
+    ctx = prope_context[:, -nf:].to(x.dtype)
+    if mode == "P_inv":
+        ctx = _invert_se3(ctx)
+    xv = x.permute(0, 2, 1, 3).reshape(B, H, nf, frame_seqlen, D // 4, 4)
+    y = torch.matmul(ctx[:, None, :, None, None], xv.unsqueeze(-1)).squeeze(-1)
+    return y.reshape(B, H, L, D).permute(0, 2, 1, 3)
 
 
 def _cache_local_size(local_attn_size):
@@ -122,7 +175,10 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         c_all = torch.cat([R_flat, t_vec], dim=-1)
         T_half = s // frame_seqlen
         delta = self.pose_mlp(c_all[:, -T_half:])                  # [B, T, d/2] per-frame phase
-        v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen)
+        if fused:
+            v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen)
+        else:
+            v_p = _se3_torch(v, prope_context, "P_inv", frame_seqlen)
         v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
         if fused:
             v_rows = v.flatten(2)
@@ -166,13 +222,24 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         s0 = max(0, local_end - self.max_attention_size)
         k_slice = kv_cache["k"][:, s0:local_end]
         v_slice = kv_cache["v"][:, s0:local_end]
+    if fused and prope_context is not None:
+        # [y | P y] in one buffer: the attention writes y, the SE3 kernel P y, one GEMM does
+        # o(y) + prope_proj(P y) (action_model.py:307-318)
+        C = n * d
+        yy = torch.empty((b, s, 2 * C), dtype=torch.bfloat16, device=x.device)
+        y = yy[..., :C].view(b, s, n, d)
+        chunk_attention(q, k_slice, v_slice, rope=rope, out=y)
+        se3_block_apply(y, prope_context, "P", frame_seqlen, out=yy[..., C:].view(b, s, n, d))
+        kv_cache["global_end_index"].fill_(cur_end)
+        kv_cache["local_end_index"].fill_(local_end)
+        return torch.nn.functional.linear(yy, *_stacked_out(self))
     attn_out = chunk_attention(q, k_slice, v_slice, rope=rope).to(x.dtype)
     kv_cache["global_end_index"].fill_(cur_end)
     kv_cache["local_end_index"].fill_(local_end)
 
     out = self.o(attn_out.flatten(2))
     if prope_context is not None:
-        x_p = se3_block_apply(attn_out, prope_context, "P", frame_seqlen)
+        x_p = _se3_torch(attn_out, prope_context, "P", frame_seqlen)
         out = out + self.prope_proj(x_p.flatten(2))
     return out
 

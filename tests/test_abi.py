@@ -81,6 +81,15 @@ def test_other_entry_points_reject_bad_arguments():
     assert fn(*ok8, 1, 8, 2, 128, -1, 1e-6, 1e-6, *s15, None, None, None) == -1           # dst_start < 0
     assert fn(*([ctypes.c_void_p(18)] + ok8[1:]), 1, 8, 2, 128, 0, 1e-6, 1e-6, *s15, None, None, None) == -1
     assert fn(*ok8, 1, 8, 2, 128, 0, 1e-6, 1e-6, *(s15[:1] + [12] + s15[2:]), None, None, None) == -1  # row stride % 8
+    # rw_se3_block_apply
+    se = lib.rw_se3_block_apply
+    s6 = [0, 256, 128, 0, 256, 128]
+    assert se(p, p, p, 1, 0, 2, 128, 20, *s6, None) == 0                  # L = 0: nothing to do
+    assert se(None, p, p, 1, 40, 2, 128, 20, *s6, None) == -1             # null pointer
+    assert se(p, p, p, 1, 40, 2, 64, 20, *s6, None) == -2                 # head_dim 64
+    assert se(p, p, p, 1, 50, 2, 128, 20, *s6, None) == -1                # partial frame
+    assert se(p, p, ctypes.c_void_p(72), 1, 40, 2, 128, 20, *s6, None) == -1   # misaligned matrices
+    assert se(p, p, p, 1, 40, 2, 128, 20, 0, 260, 128, 0, 256, 128, None) == -1  # stride % 8
 
 
 def test_import_fails_loudly_without_library(monkeypatch, tmp_path):
