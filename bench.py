@@ -449,7 +449,51 @@ def gpu_side_baselines(ro, dev):
     out["gather_gbs"] = round(nbytes / (msg * 1e-3) / 1e9, 1)
     out["qkv_norm_rope_store"] = qkv_norm_measure(ro, dev, timeit)
     out["se3_block_apply"] = se3_measure(ro, dev, timeit)
+    out["host_tier"] = host_tier_measure(dev)
+    # the DiT block's text cross-attention: the chunk's queries over 512 cached text keys
+    kt = torch.randn(1, 512, HEADS, HEAD_DIM, device=dev).to(torch.bfloat16)
+    vt = torch.randn(1, 512, HEADS, HEAD_DIM, device=dev).to(torch.bfloat16)
+    msx = timeit(lambda: chunk_attention(q, kt, vt))
+    out["text_cross_attn_ms"] = round(msx, 4)
+    out["text_cross_attn_tflops"] = round(attn_flops(CT, 512, HEADS) / msx / 1e9, 1)
     return out
+
+
+def host_tier_measure(dev, n_layers=2, chunks=20):
+    """The bank with pinned-host master copies (the reference's default direct
+    mode, and the staged hot set) at the chunk shape, on a 2-layer stack to bound
+    the pinned host pool: per chunk step (pack, decision, write-through, prefetch,
+    assembly of sink | recent | bank[R] into each layer's cache) timed on the
+    compute stream after the bank is full, and the host-to-device bytes it moved."""
+    from reworld_b200.landmark import LandmarkBankStack
+    from reworld_b200.poses import random_walk
+    res = {}
+    poses = random_walk(chunks + 2, seed=5, revisit_every=4)
+    for mode, hot in (("direct", 0), ("staged", N_LANDMARK)):
+        st = LandmarkBankStack(CT, n_layers, HEADS, HEAD_DIM, n_sink=N_SINK, recent_w=RECENT_W, K=8,
+                               retrieve_k=N_LANDMARK, device=dev, host_tier=True, hot_gpu=hot)
+        src = [torch.randn(2, CT, HEADS, HEAD_DIM, device=dev).to(torch.bfloat16) for _ in range(n_layers)]
+        caps = [torch.zeros(1, (BUDGET + 1) * CT, HEADS, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+                for _ in range(2 * n_layers)]
+        times, h2d = [], []
+        for c in range(chunks):
+            b0 = st.tier.counters["bytes_h2d"]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            R = st.add_chunk_from([x[0] for x in src], [x[1] for x in src], poses[c], poses[c + 1])
+            st.write_into_caches(caps[:n_layers], caps[n_layers:], R)
+            e1.record()
+            torch.cuda.synchronize()
+            if c >= N_SINK + RECENT_W + 8:          # bank full: steady state
+                times.append(e0.elapsed_time(e1))
+                h2d.append(st.tier.counters["bytes_h2d"] - b0)
+        ms = statistics.median(times)
+        res[mode] = {"ms_per_chunk": round(ms, 3), "h2d_bytes_per_chunk": int(statistics.median(h2d)),
+                     "h2d_gbs": round(statistics.median(h2d) / (ms * 1e-3) / 1e9, 1), "hot_gpu": hot}
+        del st
+    res["config"] = (f"{n_layers} layers x [{CT}, {HEADS}, {HEAD_DIM}] bf16 K and V per chunk, bank K = 8, "
+                     f"retrieve {N_LANDMARK}, sink {N_SINK}, recent {RECENT_W}; median of the steady-state chunks")
+    return res
 
 
 def _graph(dev, fn, n):

@@ -15,9 +15,14 @@ whose decisions are identical across layers).
 
 Storage: chunk K/V live in a device pool of slots [n_slots, n_layers, 2, ct, H,
 D] (bf16); sink, recent and bank members each own a slot, recycled through a
-free list (the reference keeps bank members in a host pool and copies them in
-over PCIe each chunk; here every member stays resident in HBM).
+free list, so by default every member stays resident in HBM (a 30-member bank
+of the 5B model is 29 GB).  With host_tier=True the bank members' master copies
+live in a pinned host pool instead, as in the reference's _TieredMemberStore
+(landmark_cache_v2.py:137-411): write-through D2H on admission, an LRU hot set
+of device slots, H2D prefetch of the retrieved members on a dedicated stream,
+or (hot_gpu = 0) direct host-to-cache copies.
 """
+import collections
 import ctypes
 import math
 import os
@@ -146,11 +151,18 @@ class _ChunkPool:
         self.free = list(range(n_slots))
         self.ct, self.H, self.D, self.n_layers = ct, H, D, n_layers
         self.chunk_bytes = ct * H * D * self.pool.element_size()
+        self.ev = {}   # slot -> last event of a copy stream that read or wrote it (host tier)
 
-    def acquire(self):
+    def acquire(self, stream=None):
+        """A free slot; `stream` (the one that will write it) first waits for the
+        slot's last use on a copy stream."""
         if not self.free:
             raise RuntimeError("chunk pool exhausted")
-        return self.free.pop(0)
+        slot = self.free.pop(0)
+        ev = self.ev.get(slot)
+        if ev is not None and stream is not None:
+            stream.wait_event(ev)
+        return slot
 
     def release(self, slot):
         self.free.append(slot)
@@ -174,6 +186,157 @@ def copy_jobs(jobs, device, status=None):
     # reused before the copy kernel (queued earlier on the same stream) has read it.
 
 
+class _HostTier:
+    """Pinned host master copies of the bank members and the device hot set.
+
+    Same protocol as the reference's _TieredMemberStore
+    (longctx/inference/landmark_cache_v2.py:137-411): put = write-through D2H on
+    a dedicated stream, the admitted chunk's device slot kept as a warm hot
+    entry; prefetch = H2D of misses on a second stream into device slots, each
+    transfer tracked by an event; an LRU hot set of hot_capacity members (the
+    host copy is the master, so dropping a hot entry needs no copy back);
+    hot_capacity 0 = direct mode (members go host -> cache rows on the compute
+    stream).  A member is one contiguous [n_layers, 2, ct, H, D] block on both
+    sides, so each transfer is one cudaMemcpyAsync.  No CPU waits: every reuse of
+    a host or device slot is ordered by events."""
+
+    def __init__(self, n_slots, pool, hot_capacity):
+        member = tuple(pool.pool.shape[1:])
+        self.host = torch.empty((n_slots,) + member, dtype=pool.pool.dtype, pin_memory=True)
+        self.pool = pool
+        self.hot_capacity = hot_capacity
+        self.free = collections.deque(range(n_slots))
+        self.m2s = {}                          # member id -> host slot
+        self.slot_ev = {}                      # host slot -> last transfer event touching it
+        self.master_ev = {}                    # member id -> write-through event
+        self.fetch_ev = {}                     # member id -> H2D event of its hot copy
+        self.hot = collections.OrderedDict()   # member id -> device slot, LRU first
+        dev = pool.pool.device
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.member_bytes = pool.pool[0].numel() * pool.pool.element_size()
+        self.counters = dict(hits=0, misses=0, warm_inserts=0, hot_evictions=0, bytes_h2d=0, bytes_d2h=0,
+                             waits_pending=0)
+
+    @property
+    def slots_in_use(self):
+        return self.host.shape[0] - len(self.free)
+
+    def _hot_insert(self, mid, dslot):
+        old = self.hot.pop(mid, None)
+        if old is not None and old != dslot:
+            self.pool.release(old)
+        self.hot[mid] = dslot
+        while len(self.hot) > self.hot_capacity:
+            _, s = self.hot.popitem(last=False)
+            self.counters["hot_evictions"] += 1
+            self.pool.release(s)               # host is master: no copy back
+
+    def put(self, mid, dslot):
+        """Admits member mid from device slot dslot (written on the compute stream)."""
+        if not self.free:
+            raise RuntimeError("host tier: no free slot (evict a bank member first)")
+        hs = self.free.popleft()
+        comp = torch.cuda.current_stream(self.pool.pool.device)
+        self.d2h.wait_stream(comp)                      # the chunk is fully packed
+        prev = self.slot_ev.get(hs)
+        if prev is not None:
+            self.d2h.wait_event(prev)                   # last read of the host slot is done
+        with torch.cuda.stream(self.d2h):
+            self.host[hs].copy_(self.pool.pool[dslot], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.d2h)
+        self.slot_ev[hs] = ev
+        self.master_ev[mid] = ev
+        self.pool.ev[dslot] = ev                        # the next writer of dslot waits for this read
+        self.m2s[mid] = hs
+        self.counters["bytes_d2h"] += self.member_bytes
+        if self.hot_capacity > 0:
+            self._hot_insert(mid, dslot)                # warm: the original device copy
+            self.counters["warm_inserts"] += 1
+        else:
+            self.pool.release(dslot)
+
+    def free_member(self, mid):
+        """Bank eviction: the host slot returns to the free list (its next writer
+        waits for its last transfer) and a hot copy is dropped."""
+        self.free.append(self.m2s.pop(mid))
+        self.master_ev.pop(mid, None)
+        self.fetch_ev.pop(mid, None)
+        s = self.hot.pop(mid, None)
+        if s is not None:
+            self.pool.release(s)
+
+    def prefetch(self, mids):
+        """H2D of the members not in the hot set, on the h2d stream; returns at once."""
+        if self.hot_capacity <= 0:
+            return
+        comp = torch.cuda.current_stream(self.pool.pool.device)
+        waited = False
+        for mid in mids:
+            if mid in self.hot:
+                self.hot.move_to_end(mid)
+                self.counters["hits"] += 1
+                continue
+            self.counters["misses"] += 1
+            if not waited:
+                self.h2d.wait_stream(comp)              # reads of recycled device slots queued so far
+                waited = True
+            ds = self.pool.acquire(self.h2d)
+            hs = self.m2s[mid]
+            mev = self.master_ev.get(mid)
+            if mev is not None:
+                self.h2d.wait_event(mev)                # the master copy has landed
+            with torch.cuda.stream(self.h2d):
+                self.pool.pool[ds].copy_(self.host[hs], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.h2d)
+            self.slot_ev[hs] = ev
+            self.pool.ev[ds] = ev
+            self.fetch_ev[mid] = ev
+            self._hot_insert(mid, ds)
+            self.counters["bytes_h2d"] += self.member_bytes
+
+    def device_slot(self, mid):
+        """The hot copy's device slot, with the compute stream ordered after its fetch."""
+        ev = self.fetch_ev.pop(mid, None)
+        if ev is not None:
+            if not ev.query():
+                self.counters["waits_pending"] += 1
+            torch.cuda.current_stream(self.pool.pool.device).wait_event(ev)
+        self.hot.move_to_end(mid)
+        return self.hot[mid]
+
+    def copy_to_rows(self, mid, layer, dst_k, dst_v):
+        """Direct mode: one member's K and V of one layer from the host slot into
+        cache rows, on the compute stream."""
+        comp = torch.cuda.current_stream(self.pool.pool.device)
+        mev = self.master_ev.get(mid)
+        if mev is not None:
+            comp.wait_event(mev)
+        hs = self.m2s[mid]
+        dst_k.copy_(self.host[hs, layer, 0], non_blocking=True)
+        dst_v.copy_(self.host[hs, layer, 1], non_blocking=True)
+
+    def mark_read(self, mids):
+        """After direct copies on the compute stream: the next write-through into
+        these members' host slots waits for them."""
+        if not mids:
+            return
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.pool.pool.device))
+        for mid in mids:
+            self.slot_ev[self.m2s[mid]] = ev
+            self.counters["misses"] += 1
+            self.counters["bytes_h2d"] += self.member_bytes
+
+    def stats(self):
+        d = dict(host_slots_used=self.slots_in_use, host_slots_total=self.host.shape[0], pinned=True,
+                 hot=len(self.hot), hot_capacity=self.hot_capacity)
+        d.update({f"io_{k}": v for k, v in self.counters.items()})
+        return d
+
+
 class LandmarkBankStack:
     """Landmark bank shared by all layers (one decision per chunk, one gather
     launch for every layer).  Same policy as LandmarkCacheV2: sink chunks,
@@ -182,15 +345,30 @@ class LandmarkBankStack:
     pose retrieval (mode 'b') or the whole bank (mode 'a')."""
 
     def __init__(self, chunk_tokens, n_layers, num_heads, head_dim, n_sink=1, recent_w=5, K=30, retrieve_k=6,
-                 mode="b", protect_n=2, device="cuda", dtype=torch.bfloat16):
+                 mode="b", protect_n=2, device="cuda", dtype=torch.bfloat16, host_tier=False, hot_gpu=None,
+                 gpu_spare=None):
+        """host_tier=True keeps the bank members' master copies in pinned host
+        memory (the reference's tiered store): hot_gpu None or 0 = direct mode
+        (members copied host -> cache rows each chunk, no device copies of the
+        bank); hot_gpu > 0 = an LRU hot set of max(hot_gpu, retrieve_k) device
+        slots plus gpu_spare (default retrieve_k) staging slots, filled by H2D
+        prefetch right after each decision."""
         _check_env()
         assert mode in ("a", "b")
         self.ct, self.n_layers, self.H, self.D = chunk_tokens, n_layers, num_heads, head_dim
         self.n_sink, self.recent_w, self.K, self.retrieve_k, self.mode = n_sink, recent_w, K, retrieve_k, mode
         self.protect_n = protect_n
         self.device = torch.device(device)
-        self.pool = _ChunkPool(n_sink + recent_w + K + 1, n_layers, chunk_tokens, num_heads, head_dim,
-                               self.device, dtype)
+        self.tier = None
+        if host_tier:
+            hot = 0 if not hot_gpu or int(hot_gpu) <= 0 else max(int(hot_gpu), retrieve_k)
+            spare = 0 if hot == 0 else (int(gpu_spare) if gpu_spare is not None else retrieve_k)
+            n_dev = n_sink + recent_w + 1 + hot + max(spare, 1 if hot else 0)
+        else:
+            n_dev = n_sink + recent_w + K + 1
+        self.pool = _ChunkPool(n_dev, n_layers, chunk_tokens, num_heads, head_dim, self.device, dtype)
+        if host_tier:
+            self.tier = _HostTier(K, self.pool, hot)
         self.dec = DeviceBankDecisions(K, retrieve_k, mode, protect_n, self.device)
         self.sink, self.recent, self.bank = [], [], []
         self.events = []
@@ -203,7 +381,7 @@ class LandmarkBankStack:
         and runs the bank decision.  Returns R (bank indices, ascending)."""
         c = self._n
         self._n += 1
-        slot = self.pool.acquire()
+        slot = self.pool.acquire(torch.cuda.current_stream(self.device))
         jobs = []
         nb = self.pool.chunk_bytes
         for layer in range(self.n_layers):
@@ -230,12 +408,20 @@ class LandmarkBankStack:
         for born, slot_ev in evicted:
             j = [m.born for m in self.bank].index(born)
             self.bank.pop(j)
-            self.pool.release(slot_ev)
+            if self.tier is not None:
+                self.tier.free_member(born)
+            else:
+                self.pool.release(slot_ev)
             self.events.append(("evict", born))
         if admit is not None:
             admit.protected = self.dec._admitted <= self.protect_n
+            if self.tier is not None:
+                self.tier.put(admit.born, admit.slot)   # the device slot now belongs to the tier
+                admit.slot = None
             self.bank.append(admit)
             self.events.append(("add", admit.born, len(self.bank)))
+        if self.tier is not None:
+            self.tier.prefetch([self.bank[i].born for i in R])   # overlaps the next chunk's compute
         return R
 
     # -- cache assembly ------------------------------------------------------
@@ -251,7 +437,13 @@ class LandmarkBankStack:
         if tot == 0:
             return 0
         nb = self.pool.chunk_bytes
-        jobs = []
+        # device slot of every chunk; None = a bank member read from the host tier (direct mode)
+        slots = [ch.slot for ch in chunks]
+        if self.tier is not None:
+            for i, ch in enumerate(chunks):
+                if ch.slot is None and self.tier.hot_capacity > 0:
+                    slots[i] = self.tier.device_slot(ch.born)
+        jobs, direct = [], []
         for layer in range(self.n_layers):
             ck, cv = caches_k[layer], caches_v[layer]
             ck2 = ck[0] if ck.dim() == 4 else ck
@@ -263,33 +455,54 @@ class LandmarkBankStack:
             row = ck2.stride(0) * ck2.element_size()
             for i, ch in enumerate(chunks):
                 dst = (offset + i * self.ct) * row
-                jobs.append((self.pool.ptr(ch.slot, layer, 0), ck2.data_ptr() + dst, nb))
-                jobs.append((self.pool.ptr(ch.slot, layer, 1), cv2.data_ptr() + dst, nb))
+                if slots[i] is None:
+                    r0 = offset + i * self.ct
+                    direct.append((ch.born, layer, ck2[r0:r0 + self.ct], cv2[r0:r0 + self.ct]))
+                    continue
+                jobs.append((self.pool.ptr(slots[i], layer, 0), ck2.data_ptr() + dst, nb))
+                jobs.append((self.pool.ptr(slots[i], layer, 1), cv2.data_ptr() + dst, nb))
         copy_jobs(jobs, self.device)
+        for born, layer, dk, dv in direct:
+            self.tier.copy_to_rows(born, layer, dk, dv)
+        if direct:
+            self.tier.mark_read(sorted({d[0] for d in direct}))
         return tot
 
     def stats(self, R):
-        return dict(sink=len(self.sink), recent=len(self.recent), bank=len(self.bank),
-                    attended=len(self.sink) + len(self.recent) + len(R),
-                    pool_slots_used=self.pool.pool.shape[0] - len(self.pool.free),
-                    pool_slots_total=self.pool.pool.shape[0])
+        d = dict(sink=len(self.sink), recent=len(self.recent), bank=len(self.bank),
+                 attended=len(self.sink) + len(self.recent) + len(R),
+                 pool_slots_used=self.pool.pool.shape[0] - len(self.pool.free),
+                 pool_slots_total=self.pool.pool.shape[0])
+        if self.tier is not None:
+            d.update(self.tier.stats())
+        return d
 
 
 class LandmarkCacheV2:
     """Per-layer drop-in for longctx/inference/landmark_cache_v2.py:413 LandmarkCacheV2.
 
-    Same constructor (eps / diverse / hot_gpu / gpu_spare are accepted for
-    compatibility and have no effect: there is no host tier) and the same
-    methods.  K/V are device tensors; the pool is created at the first
-    add_chunk from the chunk's shape."""
+    Same constructor (eps / diverse are accepted for compatibility and have no
+    effect, as in the reference's v2) and the same methods.  K/V are device
+    tensors; the pool is created at the first add_chunk from the chunk's shape.
+    By default every bank member stays in HBM.  host_tier=True selects the
+    reference's tiered store: hot_gpu / gpu_spare (or BANKV2_HOT_GPU /
+    BANKV2_GPU_SPARE, read as the reference reads them,
+    landmark_cache_v2.py:431-451) choose direct mode (hot_gpu None or 0) or the
+    staged hot set."""
 
     def __init__(self, chunk_tokens, n_sink=1, recent_w=5, K=30, retrieve_k=6, eps=0.5, mode="b", diverse=False,
-                 protect_n=2, hot_gpu=None, gpu_spare=None):
+                 protect_n=2, hot_gpu=None, gpu_spare=None, host_tier=False):
         _check_env()
         assert mode in ("a", "b")
         self.ct, self.n_sink, self.recent_w, self.K = chunk_tokens, n_sink, recent_w, K
         self.retrieve_k, self.mode, self.protect_n = retrieve_k, mode, protect_n
         self.eps, self.diverse = eps, diverse
+        if host_tier:
+            if hot_gpu is None and os.environ.get("BANKV2_HOT_GPU"):
+                hot_gpu = int(os.environ["BANKV2_HOT_GPU"])
+            if gpu_spare is None and os.environ.get("BANKV2_GPU_SPARE"):
+                gpu_spare = int(os.environ["BANKV2_GPU_SPARE"])
+        self.host_tier, self.hot_gpu, self.gpu_spare = host_tier, hot_gpu, gpu_spare
         self._stack = None
         self.events = []
 
@@ -299,7 +512,9 @@ class LandmarkCacheV2:
             if ct != self.ct:
                 raise ValueError(f"chunk has {ct} tokens, expected {self.ct}")
             self._stack = LandmarkBankStack(ct, 1, H, D, self.n_sink, self.recent_w, self.K, self.retrieve_k,
-                                            self.mode, self.protect_n, device=k.device, dtype=k.dtype)
+                                            self.mode, self.protect_n, device=k.device, dtype=k.dtype,
+                                            host_tier=self.host_tier, hot_gpu=self.hot_gpu,
+                                            gpu_spare=self.gpu_spare)
             self._stack.events = self.events
 
     @property
@@ -332,9 +547,23 @@ class LandmarkCacheV2:
         chunks = self.active_layout(R)
         if not chunks:
             return None, None, 0
-        pool = self._stack.pool.pool
-        k = torch.cat([pool[c.slot, 0, 0] for c in chunks], 0)
-        v = torch.cat([pool[c.slot, 0, 1] for c in chunks], 0)
+        st = self._stack
+        pool = st.pool.pool
+        parts = []
+        for c in chunks:
+            if c.slot is not None:
+                parts.append(pool[c.slot, 0])
+            elif st.tier.hot_capacity > 0:
+                parts.append(pool[st.tier.device_slot(c.born), 0])
+            else:
+                mev = st.tier.master_ev.get(c.born)
+                if mev is not None:
+                    torch.cuda.current_stream(st.device).wait_event(mev)
+                parts.append(st.tier.host[st.tier.m2s[c.born], 0].to(st.device, non_blocking=True))
+        k = torch.cat([p_[0] for p_ in parts], 0)
+        v = torch.cat([p_[1] for p_ in parts], 0)
+        if st.tier is not None and st.tier.hot_capacity == 0:
+            st.tier.mark_read([c.born for c in chunks if c.slot is None])
         return k, v, k.shape[0]
 
     def stats(self, R):

@@ -194,3 +194,26 @@ def test_attention_key_split_matches_unsplit(cuda, B, Lq, Lk, H):
     err = (split.float() - whole.float()).abs()
     assert err.max().item() < 1e-2 and err.mean().item() < 1e-4
     _status_clean()
+
+
+def test_text_cross_attention_shape(cuda):
+    """The DiT block's text cross-attention (wan_5b/modules/model.py:164-197 and the
+    multi-shot form, causal_model.py:186-289): the chunk's 2640 queries over the
+    cached 512 text keys, context_lens restricting the keys per batch element
+    (flash_attention(q, k, v, k_lens=context_lens)), against an fp32 reference."""
+    from reworld_b200 import attention
+    g = torch.Generator(device=cuda).manual_seed(21)
+    B, Lq, Lk, H = 2, 2640, 512, 24
+    q = torch.randn(B, Lq, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    lens = torch.tensor([512, 77], device=cuda)
+    out = attention(q, k, v, k_lens=lens)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (0, 17), (1, 5), (1, 23)):
+        n = int(lens[b])
+        qh, kh, vh = q[b, :, h].float(), k[b, :n, h].float(), v[b, :n, h].float()
+        ref = torch.softmax((qh @ kh.T) / math.sqrt(128), dim=-1) @ vh
+        err = (out[b, :, h].float() - ref).abs()
+        assert err.max().item() < MAX_ABS and err.mean().item() < MEAN_ABS, (b, h)
+    _status_clean()
