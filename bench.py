@@ -456,7 +456,39 @@ def gpu_side_baselines(ro, dev):
     msx = timeit(lambda: chunk_attention(q, kt, vt))
     out["text_cross_attn_ms"] = round(msx, 4)
     out["text_cross_attn_tflops"] = round(attn_flops(CT, 512, HEADS) / msx / 1e9, 1)
+    out["block_ffn"] = ffn_measure(dev, timeit)
     return out
+
+
+def ffn_measure(dev, timeit, ffn_dim=14336):
+    """The DiT block's norm2 + FFN on one layer's chunk [2640, 3072]: the LayerNorm row
+    kernel, and GeluFFN (GELU in the first GEMM's cuBLASLt epilogue) against the
+    reference's Linear -> GELU(tanh) -> Linear, both on the same bf16 weights."""
+    import torch.nn as nn
+    from reworld_b200.block import GeluFFN, row_norm
+    C = HEADS * HEAD_DIM
+    seq = nn.Sequential(nn.Linear(C, ffn_dim), nn.GELU(approximate="tanh"), nn.Linear(ffn_dim, C))
+    seq = seq.to(device=dev, dtype=torch.bfloat16)
+    fused = GeluFFN(seq)
+    xs = [torch.randn(1, CT, C, device=dev).to(torch.bfloat16) for _ in range(8)]
+    it = [0]
+
+    def nxt():
+        it[0] += 1
+        return xs[it[0] % len(xs)]
+
+    with torch.no_grad():
+        ms_f = timeit(lambda: fused(nxt()), n=10)
+        ms_u = timeit(lambda: seq(nxt()), n=10)
+        ms_n = timeit(lambda: row_norm(nxt(), None, None, 1e-6, "layer"), n=20)
+    fl = 2 * 2 * CT * C * ffn_dim
+    burst, sustained, hbm, peak_src = load_peaks()
+    nb = 2 * CT * C * 2
+    return {"ffn_ms": round(ms_f, 4), "ffn_tflops": round(fl / ms_f / 1e9, 1),
+            "frac_of_bf16_burst": round(fl / ms_f / 1e9 / burst, 4), "unfused_ffn_ms": round(ms_u, 4),
+            "layer_norm_ms": round(ms_n, 4), "layer_norm_gbs": round(nb / (ms_n * 1e-3) / 1e9, 1),
+            "shape": f"[{CT}, {C}] -> {ffn_dim} -> {C}, bf16; inputs rotate over 8 chunks",
+            "peak_kind": f"cuBLAS bf16 burst ({peak_src})"}
 
 
 def host_tier_measure(dev, n_layers=2, chunks=20):

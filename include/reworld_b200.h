@@ -148,6 +148,20 @@ int rw_se3_block_apply(const void* x, void* out, const float* mats, int B, int L
                        long long x_sb, long long x_sl, long long x_sh, long long o_sb, long long o_sl,
                        long long o_sh, void* stream);
 
+/* Row normalisations of the DiT block on bf16 rows [rows, C] (row strides in
+ * elements, multiples of 8; C a multiple of 8):
+ *   RW_NORM_RMS    WanRMSNorm (wan_5b/modules/model.py:73-89): y = bf16(bf16(x * r) * w),
+ *                  r = 1 / sqrt(mean(x^2) + eps); w (bf16 [C]) required, b must be NULL.
+ *                  The cross-attention's norm_q (model.py:175, causal_model.py:218).
+ *   RW_NORM_LAYER  WanLayerNorm (model.py:92-102): y = bf16((x - mean) * rstd * w + b) with
+ *                  w, b optional (elementwise_affine off: both NULL).  norm2 / norm3 of
+ *                  the block (action_model.py:399-403, 547-553).
+ * fp32 statistics; HBM-bound, one warp per row. */
+#define RW_NORM_RMS 0
+#define RW_NORM_LAYER 1
+int rw_row_norm(const void* x, void* out, const void* w, const void* b, long long rows, int C, long long x_row_stride,
+                long long out_row_stride, float eps, int mode, void* stream);
+
 /* One byte-copy job of the landmark/cache assembly: nbytes from src to dst,
  * both 16-byte aligned, nbytes a multiple of 16. */
 typedef struct rw_copy_desc {

@@ -56,6 +56,7 @@ _SIGNATURES = {
     "rw_qkv_norm_rope_store": (c_int, [c_vp] * 8 + [c_int] * 5 + [c_float] * 2 + [c_ll] * 15
                                + [ctypes.POINTER(RwRope), c_vp, c_vp]),
     "rw_se3_block_apply": (c_int, [c_vp] * 3 + [c_int] * 5 + [c_ll] * 6 + [c_vp]),
+    "rw_row_norm": (c_int, [c_vp] * 4 + [c_ll, c_int, c_ll, c_ll, c_float, c_int, c_vp]),
     "rw_copy_chunks": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "rw_bank_step": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp]),
     "rw_a2a_pack": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),

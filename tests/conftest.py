@@ -24,4 +24,4 @@ def cuda():
 def golden():
     import numpy as np
     d = os.path.join(ROOT, "tests", "golden")
-    return {n: np.load(os.path.join(d, n + ".npz")) for n in ("attention", "rope", "rmsnorm", "self_attn", "landmark", "ulysses")}
+    return {n: np.load(os.path.join(d, n + ".npz")) for n in ("attention", "rope", "rmsnorm", "block", "self_attn", "landmark", "ulysses")}

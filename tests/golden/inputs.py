@@ -45,6 +45,32 @@ def rmsnorm_case():
     return x, wq, wk
 
 
+BLOCK_DIM, BLOCK_HEADS, BLOCK_FFN = 256, 2, 512   # reduced width of the DiT block's cross-attn + FFN
+BLOCK_FRAMES, BLOCK_FS, BLOCK_CTX = 2, 20, 16      # frames x tokens per frame; text tokens
+
+
+def block_params(param_shapes):
+    """Parameter values in sorted-name order (weights N(0, 0.05), norm weights 1 + N(0, 0.05))."""
+    g = torch.Generator().manual_seed(31)
+    vals = {}
+    for name, shape in sorted(param_shapes.items()):
+        if name.endswith("norm_q.weight") or name.endswith("norm_k.weight") or name == "norm3.weight":
+            vals[name] = 1.0 + torch.randn(shape, generator=g) * 0.05
+        else:
+            vals[name] = torch.randn(shape, generator=g) * 0.05
+    return vals
+
+
+def block_inputs():
+    """x [1, F*fs, dim], context [1, ctx, dim] and the block's modulation e [1, F, 6, dim], bf16."""
+    g = torch.Generator().manual_seed(32)
+    L = BLOCK_FRAMES * BLOCK_FS
+    x = torch.randn(1, L, BLOCK_DIM, generator=g).to(torch.bfloat16)
+    context = torch.randn(1, BLOCK_CTX, BLOCK_DIM, generator=g).to(torch.bfloat16)
+    e = (torch.randn(1, BLOCK_FRAMES, 6, BLOCK_DIM, generator=g) * 0.1).to(torch.bfloat16)
+    return x, context, e
+
+
 def attention_case(i):
     B, Lq, Lk, H = ATTN_CASES[i]
     g = torch.Generator().manual_seed(100 + i)

@@ -20,6 +20,8 @@ tests); each fixture keeps a checksum of its inputs and the reference's outputs:
   landmark.npz      LandmarkCacheV2 runs: retrieved index lists, bank contents,
                     events and write_into_cache bytes of the last chunks
   rmsnorm.npz       WanRMSNorm (the q/k norms) on bf16 rows of the 5B width
+  block.npz         the DiT block's cross_attn_ffn (norm3, MultiShotT2VCrossAttention,
+                    norm2 + modulation, FFN, gated residuals) at reduced width, bf16
   ulysses.npz       wan_5b/distributed/util.all_to_all (seq->head and back)
                     over gloo process groups of 2 and 4 ranks (gloo lacks
                     all_to_all; it is emulated by its definition with all_gather)
@@ -111,6 +113,42 @@ def gen_rmsnorm():
         with torch.no_grad():
             out[f"norm_{tag}"] = bits(norm(x))
     np.savez_compressed(os.path.join(HERE, "rmsnorm.npz"), **out)
+
+
+def gen_block(att):
+    import torch.nn as nn
+    import wan_5b.modules.causal_model as cm
+    from wan_5b.modules.model import WanLayerNorm
+    cm.flash_attention = att.attention   # CPU: the reference's SDPA branch (no flash-attention wheel)
+    dim, H, ffn_dim = gi.BLOCK_DIM, gi.BLOCK_HEADS, gi.BLOCK_FFN
+    mods = nn.ModuleDict({
+        "norm3": WanLayerNorm(dim, 1e-6, elementwise_affine=True),
+        "cross_attn": cm.MultiShotT2VCrossAttention(dim, H, (-1, -1), True, 1e-6),
+        "norm2": WanLayerNorm(dim, 1e-6),
+        "ffn": nn.Sequential(nn.Linear(dim, ffn_dim), nn.GELU(approximate="tanh"), nn.Linear(ffn_dim, dim)),
+    })
+    shapes = {n: tuple(p.shape) for n, p in mods.named_parameters()}
+    vals = gi.block_params(shapes)
+    with torch.no_grad():
+        for n, p in mods.named_parameters():
+            p.copy_(vals[n])
+    mods = mods.to(torch.bfloat16)
+    x, context, e_mod = gi.block_inputs()
+    F, fs = gi.BLOCK_FRAMES, gi.BLOCK_FS
+    lens = torch.tensor([gi.BLOCK_CTX])
+    e = e_mod.chunk(6, dim=2)
+    with torch.no_grad():
+        # the block's cross_attn_ffn (action_model.py:547-556), with the reference's modules
+        n3 = mods["norm3"](x)
+        ca = mods["cross_attn"](n3, context, lens)
+        x1 = x + ca
+        n2 = mods["norm2"](x1)
+        y = mods["ffn"]((n2.unflatten(dim=1, sizes=(F, fs)) * (1 + e[4]) + e[3]).flatten(1, 2))
+        x2 = x1 + (y.unflatten(dim=1, sizes=(F, fs)) * e[5]).flatten(1, 2)
+    out = {"checksum": np.array(gi.checksum(*[vals[n] for n in sorted(vals)], x, context, e_mod))}
+    for name, t in (("norm3", n3), ("cross_attn", ca), ("x1", x1), ("norm2", n2), ("ffn", y), ("out", x2)):
+        out[name] = bits(t)
+    np.savez_compressed(os.path.join(HERE, "block.npz"), **out)
 
 
 def gen_self_attn(att):
@@ -241,13 +279,15 @@ def main():
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     att = setup_reference(a.reference)
-    todo = a.only.split(",") if a.only else ["attention", "rope", "rmsnorm", "self_attn", "landmark", "ulysses"]
+    todo = a.only.split(",") if a.only else ["attention", "rope", "rmsnorm", "block", "self_attn", "landmark", "ulysses"]
     if "attention" in todo:
         gen_attention(att)
     if "rope" in todo:
         gen_rope()
     if "rmsnorm" in todo:
         gen_rmsnorm()
+    if "block" in todo:
+        gen_block(att)
     if "self_attn" in todo:
         gen_self_attn(att)
     if "landmark" in todo:

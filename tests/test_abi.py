@@ -90,6 +90,15 @@ def test_other_entry_points_reject_bad_arguments():
     assert se(p, p, p, 1, 50, 2, 128, 20, *s6, None) == -1                # partial frame
     assert se(p, p, ctypes.c_void_p(72), 1, 40, 2, 128, 20, *s6, None) == -1   # misaligned matrices
     assert se(p, p, p, 1, 40, 2, 128, 20, 0, 260, 128, 0, 256, 128, None) == -1  # stride % 8
+    # rw_row_norm
+    rn = lib.rw_row_norm
+    assert rn(p, p, None, None, 0, 256, 256, 256, 1e-6, 1, None) == 0      # no rows
+    assert rn(None, p, None, None, 4, 256, 256, 256, 1e-6, 1, None) == -1  # null x
+    assert rn(p, p, None, None, 4, 256, 256, 256, 1e-6, 0, None) == -1     # rms needs a weight
+    assert rn(p, p, None, p, 4, 256, 256, 256, 1e-6, 1, None) == -1        # bias without weight
+    assert rn(p, p, None, None, 4, 250, 256, 256, 1e-6, 1, None) == -1     # C % 8
+    assert rn(p, p, None, None, 4, 256, 200, 256, 1e-6, 1, None) == -1     # row stride < C
+    assert rn(p, p, None, None, 4, 256, 256, 256, 1e-6, 7, None) == -1     # unknown mode
 
 
 def test_import_fails_loudly_without_library(monkeypatch, tmp_path):

@@ -47,6 +47,30 @@ def test_rmsnorm_oracle_matches_reference(golden, tag):
     assert np.array_equal(torch_bf16_to_bits(y), g[f"norm_{tag}"].reshape(x.shape))
 
 
+def _block_params_bf16():
+    import torch.nn as nn
+    dim, H, ffn = gi.BLOCK_DIM, gi.BLOCK_HEADS, gi.BLOCK_FFN
+    shapes = {"norm3.weight": (dim,), "norm3.bias": (dim,), "ffn.0.weight": (ffn, dim), "ffn.0.bias": (ffn,),
+              "ffn.2.weight": (dim, ffn), "ffn.2.bias": (dim,)}
+    for nm in ("q", "k", "v", "o"):
+        shapes[f"cross_attn.{nm}.weight"], shapes[f"cross_attn.{nm}.bias"] = (dim, dim), (dim,)
+    shapes["cross_attn.norm_q.weight"] = shapes["cross_attn.norm_k.weight"] = (dim,)
+    vals = gi.block_params(shapes)
+    return {k: v.to(torch.bfloat16) for k, v in vals.items()}, vals
+
+
+def test_block_oracle_matches_reference(golden):
+    """The oracle's cross_attn_ffn reproduces every stage of the reference block's bits."""
+    from oracle import block as ob
+    g = golden["block"]
+    W, vals = _block_params_bf16()
+    x, context, e = gi.block_inputs()
+    assert abs(gi.checksum(*[vals[n] for n in sorted(vals)], x, context, e) - float(g["checksum"])) < 1e-6
+    st = ob.cross_attn_ffn(W, x, context, e, gi.BLOCK_HEADS, gi.BLOCK_FRAMES)
+    for name in ("norm3", "cross_attn", "x1", "norm2", "ffn", "out"):
+        assert np.array_equal(torch_bf16_to_bits(st[name]), g[name].reshape(st[name].shape)), name
+
+
 def test_rope_table_matches_reference(golden):
     g = golden["rope"]
     fr = orope.build_freqs(128, gi.ROPE_SCALE_H, gi.ROPE_SCALE_W)
