@@ -156,7 +156,7 @@ int rw_se3_block_apply(const void* x, void* out, const float* mats, int B, int L
  *   RW_NORM_LAYER  WanLayerNorm (model.py:92-102): y = bf16((x - mean) * rstd * w + b) with
  *                  w, b optional (elementwise_affine off: both NULL).  norm2 / norm3 of
  *                  the block (action_model.py:399-403, 547-553).
- * fp32 statistics; HBM-bound, one warp per row. */
+ * fp32 statistics; C <= 8192; HBM-bound, one 128-thread CTA per row. */
 #define RW_NORM_RMS 0
 #define RW_NORM_LAYER 1
 int rw_row_norm(const void* x, void* out, const void* w, const void* b, long long rows, int C, long long x_row_stride,

@@ -7,10 +7,11 @@
 //                      (WanLayerNorm, model.py:92-102: torch layer_norm, statistics and
 //                       affine in fp32, one rounding), used for norm2 / norm3 of the block
 //                       (action_model.py:399-403, 547-553); w, b optional (affine off).
-// One warp per row (persistent grid); the row is read once from HBM and re-read
-// from L1 for the later passes.  The fp32 sums run in another order than torch's,
-// so an output can differ from it by a bf16 unit (two in RMS mode, where a unit
-// before the weight product can widen after it).  HBM-bound: 2 C bytes read and
+// One 128-thread CTA per row: each thread keeps its chunks of the row in
+// registers, so the row is read once; block reductions give the statistics.
+// The fp32 sums run in another order than torch's, so an output can differ from
+// it by a bf16 unit (two where a unit before the weight product, or before an
+// affine that cancels, widens after it).  HBM-bound: 2 C bytes read and
 // 2 C bytes written per row.
 #include "common.cuh"
 #include "host_util.h"
@@ -28,27 +29,38 @@ struct Params {
   float eps;
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
+constexpr int THREADS = 128;    // one CTA per row
+constexpr int MAX_PER = 8;      // 16-byte chunks per thread: C <= 8 * 8 * 128 = 8192 (PER = 3: C <= 3072)
+
+// Sum over the CTA; every thread gets the same bits (one fixed order of the
+// per-warp partials).
+__device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;  // the same bits in every lane
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();  // the previous use of red is finished
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
 }
 
-__global__ void __launch_bounds__(256) row_norm_kernel(const __grid_constant__ Params p) {
-  const int lane = threadIdx.x & 31;
-  const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+template <int PER>
+__global__ void __launch_bounds__(THREADS) row_norm_kernel(const __grid_constant__ Params p) {
+  __shared__ float red[THREADS / 32];
   const int nch = p.C / 8;
   const uint4* wv = reinterpret_cast<const uint4*>(p.w);
   const uint4* bv = reinterpret_cast<const uint4*>(p.b);
-  for (long long row = warp0; row < p.rows; row += nwarps) {
+  for (long long row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(p.x + 2 * row * p.x_rs);
     uint4* orow = reinterpret_cast<uint4*>(p.out + 2 * row * p.o_rs);
-    // pass 1: sum (layer) or sum of squares (rms)
+    // the row is read once: this thread's chunks c = threadIdx.x + 128 k stay in registers
+    uint4 v[PER];
     float s = 0.f;
-    for (int c = lane; c < nch; c += 32) {
-      const uint4 v = __ldg(xr + c);
-      const uint32_t xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int c = threadIdx.x + THREADS * k;
+      v[k] = c < nch ? __ldg(xr + c) : make_uint4(0, 0, 0, 0);
+      const uint32_t xs[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float a = bf16_lo(xs[i]), b = bf16_hi(xs[i]);
@@ -61,17 +73,18 @@ __global__ void __launch_bounds__(256) row_norm_kernel(const __grid_constant__ P
         }
       }
     }
-    s = warp_sum(s);
+    s = block_sum(s, red);
     float scale, shift = 0.f;  // y = x * scale + shift (before the affine / weight)
     if (p.mode == RW_NORM_RMS) {
       scale = 1.0f / sqrtf(s / (float)p.C + p.eps);
     } else {
       const float mean = s / (float)p.C;
-      // pass 2: variance about the mean (two-pass, population variance as layer_norm)
+      // variance about the mean (two-pass, population variance as layer_norm)
       float q = 0.f;
-      for (int c = lane; c < nch; c += 32) {
-        const uint4 v = __ldg(xr + c);
-        const uint32_t xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        if (threadIdx.x + THREADS * k >= nch) continue;
+        const uint32_t xs[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float a = bf16_lo(xs[i]) - mean, b = bf16_hi(xs[i]) - mean;
@@ -79,14 +92,15 @@ __global__ void __launch_bounds__(256) row_norm_kernel(const __grid_constant__ P
           q = __fmaf_rn(b, b, q);
         }
       }
-      q = warp_sum(q);
+      q = block_sum(q, red);
       scale = 1.0f / sqrtf(q / (float)p.C + p.eps);
       shift = -mean * scale;
     }
-    // last pass: normalise and store
-    for (int c = lane; c < nch; c += 32) {
-      const uint4 v = __ldg(xr + c);
-      const uint32_t xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int c = threadIdx.x + THREADS * k;
+      if (c >= nch) continue;
+      const uint32_t xs[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
       uint32_t ws[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
       uint32_t bs[4] = {0u, 0u, 0u, 0u};
       if (wv != nullptr) {
@@ -134,6 +148,7 @@ extern "C" int rw_row_norm(const void* x, void* out, const void* w, const void* 
   if (mode == RW_NORM_RMS && w == nullptr) return RW_ERR_INVALID_ARG;
   if (b != nullptr && w == nullptr) return RW_ERR_INVALID_ARG;
   if (rows < 0 || C < 8 || C % 8 != 0 || !(eps >= 0.f)) return RW_ERR_INVALID_ARG;
+  if (C > 8 * rown::MAX_PER * rown::THREADS) return RW_ERR_UNSUPPORTED;
   if (rows == 0) return RW_OK;
   if (!aligned16(x) || !aligned16(out) || (w && !aligned16(w)) || (b && !aligned16(b))) return RW_ERR_INVALID_ARG;
   if (x_row_stride < C || out_row_stride < C || x_row_stride % 8 != 0 || out_row_stride % 8 != 0)
@@ -152,10 +167,11 @@ extern "C" int rw_row_norm(const void* x, void* out, const void* w, const void* 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long warps_needed = rows;
-  long long grid = (warps_needed + 7) / 8;  // 8 warps per 256-thread CTA
-  const long long cap = (long long)sms * 8;
-  if (grid > cap) grid = cap;
-  rown::row_norm_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(p);
+  const long long cap = (long long)sms * 16;  // 16 resident CTAs per SM, rows strided over them
+  const long long grid = rows < cap ? rows : cap;
+  if (C <= 8 * 3 * rown::THREADS)
+    rown::row_norm_kernel<3><<<(unsigned)grid, rown::THREADS, 0, (cudaStream_t)stream>>>(p);
+  else
+    rown::row_norm_kernel<rown::MAX_PER><<<(unsigned)grid, rown::THREADS, 0, (cudaStream_t)stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
