@@ -3,9 +3,9 @@
 // Replaces wan_5b/modules/action_model.py:265-292: q_f, k_f = apply_rope(q, k,
 // delta_tok, start_f=g_start_f, ...) followed by
 // kv_cache["k"][:, local_start:local_end] = k_f and kv_cache["v"][...] = v.
-// One thread per 16-byte chunk (8 bf16 = 4 complex pairs) of a (batch, token,
-// head) row; V is a plain 16-byte copy.  HBM-bound: reads k, v (and q), writes
-// the cache rows (and roped q).
+// CTAs walk the tokens; a thread moves 16-byte chunks (8 bf16 = 4 complex
+// pairs) of the token's head rows; V is a plain 16-byte copy.  HBM-bound: reads
+// k, v (and q), writes the cache rows (and roped q).
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
@@ -20,7 +20,7 @@ struct Params {
   uint8_t* q_out;
   uint8_t* ck;
   uint8_t* cv;
-  int L, H, dst_start;
+  int B, L, H, dst_start;
   long long k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, q_sb, q_sl, q_sh, qo_sb, qo_sl, qo_sh;
   long long ck_sb, ck_sl, ck_sh, cv_sb, cv_sl, cv_sh;
   int rope_on;
@@ -32,34 +32,65 @@ __device__ __forceinline__ uint4 ldg16(const uint8_t* p) {
 }
 __device__ __forceinline__ void stg16(uint8_t* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
-__global__ void __launch_bounds__(256) rope_kv_store_kernel(const __grid_constant__ Params p) {
-  const long long n = (long long)p.L * p.H * 16;
-  const int b = blockIdx.y;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int c16 = (int)(idx & 15);
-    const long long th = idx >> 4;
-    const int h = (int)(th % p.H);
-    const int t = (int)(th / p.H);
-    const long long eoff = (long long)c16 * 8;  // element offset within the head row
-    RopeToken rt;
-    if (p.rope_on) rt = rope_token(p.rope, t, b);
-    // V: plain copy into the cache slot
-    {
+constexpr int THREADS = 128;  // a multiple of 16: a thread's chunks all sit at one place in their head
+
+// The 4 RoPE pairs of chunk position c16 of the token (same for every head).
+struct RopeRegs {
+  double2 cs[4];
+  float2 dl[4];
+  bool rot, has_d;
+};
+
+__device__ __forceinline__ void rope_regs(const rw_rope_t& rp, int t, int b, int c16, RopeRegs& r) {
+  const RopeToken rt = rope_token(rp, t, b);
+  r.rot = rt.on;
+  r.has_d = rt.dl != nullptr;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r.cs[j] = rope_freq(4 * c16 + j, rt);
+    r.dl[j] = r.has_d ? rt.dl[4 * c16 + j] : make_float2(0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ uint4 rotate(uint4 v, const RopeRegs& r) {
+  v.x = rope_rotate(v.x, r.cs[0], r.has_d, r.dl[0]);
+  v.y = rope_rotate(v.y, r.cs[1], r.has_d, r.dl[1]);
+  v.z = rope_rotate(v.z, r.cs[2], r.has_d, r.dl[2]);
+  v.w = rope_rotate(v.w, r.cs[3], r.has_d, r.dl[3]);
+  return v;
+}
+
+// CTAs walk the tokens (b, t); a thread handles the token's chunks threadIdx.x,
+// threadIdx.x + 128, ... (all at chunk position c16 = threadIdx.x mod 16 of
+// their head), so the token's position and this thread's 4 RoPE table entries
+// are looked up once per token.
+__global__ void __launch_bounds__(THREADS) rope_kv_store_kernel(const __grid_constant__ Params p) {
+  const long long tokens = (long long)p.B * p.L;
+  const int nch = p.H * 16;
+  const int c16 = threadIdx.x & 15;
+  const long long eoff = (long long)c16 * 8;  // element offset within the head row
+  for (long long tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+    const int b = (int)(tok / p.L);
+    const int t = (int)(tok - (long long)b * p.L);
+    RopeRegs r;
+    r.rot = false;
+    if (p.rope_on) rope_regs(p.rope, t, b, c16, r);
+    const long long td = (long long)p.dst_start + t;
+    for (int c = threadIdx.x; c < nch; c += THREADS) {
+      const long long h = c >> 4;
+      // V: plain copy into the cache slot
       const uint4 vv = ldg16(p.v + 2 * (b * p.v_sb + t * p.v_sl + h * p.v_sh + eoff));
-      stg16(p.cv + 2 * (b * p.cv_sb + (long long)(p.dst_start + t) * p.cv_sl + h * p.cv_sh + eoff), vv);
-    }
-    // K: rotate, then store into the cache slot
-    {
+      stg16(p.cv + 2 * (b * p.cv_sb + td * p.cv_sl + h * p.cv_sh + eoff), vv);
+      // K: rotate, then store into the cache slot
       uint4 kv = ldg16(p.k + 2 * (b * p.k_sb + t * p.k_sl + h * p.k_sh + eoff));
-      if (p.rope_on) kv = rope_chunk(kv, c16, rt);
-      stg16(p.ck + 2 * (b * p.ck_sb + (long long)(p.dst_start + t) * p.ck_sl + h * p.ck_sh + eoff), kv);
-    }
-    // Q: optional rotated copy
-    if (p.q_in != nullptr) {
-      uint4 qv = ldg16(p.q_in + 2 * (b * p.q_sb + t * p.q_sl + h * p.q_sh + eoff));
-      if (p.rope_on) qv = rope_chunk(qv, c16, rt);
-      stg16(p.q_out + 2 * (b * p.qo_sb + t * p.qo_sl + h * p.qo_sh + eoff), qv);
+      if (r.rot) kv = rotate(kv, r);
+      stg16(p.ck + 2 * (b * p.ck_sb + td * p.ck_sl + h * p.ck_sh + eoff), kv);
+      // Q: optional rotated copy
+      if (p.q_in != nullptr) {
+        uint4 qv = ldg16(p.q_in + 2 * (b * p.q_sb + t * p.q_sl + h * p.q_sh + eoff));
+        if (r.rot) qv = rotate(qv, r);
+        stg16(p.q_out + 2 * (b * p.qo_sb + t * p.qo_sl + h * p.qo_sh + eoff), qv);
+      }
     }
   }
 }
@@ -113,10 +144,13 @@ extern "C" int rw_rope_kv_store(const void* k, const void* v, const void* q_in, 
     p.rope = *rope;
     p.rope_on = 1;
   }
-  const long long n = (long long)L * H * 16;
-  long long blocks = (n + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  dim3 grid((unsigned)blocks, B);
-  store::rope_kv_store_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+  p.B = B;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tokens = (long long)B * L;
+  const long long cap = (long long)sms * 16;  // 16 resident 128-thread CTAs per SM, tokens strided over them
+  const long long grid = tokens < cap ? tokens : cap;
+  store::rope_kv_store_kernel<<<(unsigned)grid, store::THREADS, 0, (cudaStream_t)stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }

@@ -40,26 +40,49 @@ struct ScatterQKV {
   rw_rope_t rope;
 };
 
-__global__ void __launch_bounds__(256) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
-  const long long n = (long long)p.Ls * p.H * 16;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int c16 = (int)(idx & 15);
-    const long long sh = idx >> 4;
-    const int h = (int)(sh % p.H);
-    const int s = (int)(sh / p.H);
-    const int owner = h / p.Hp, hl = h - owner * p.Hp;
+constexpr int SCATTER_THREADS = 128;  // a multiple of 16 (see scatter_qkv_kernel)
+
+// CTAs walk this rank's tokens s; a thread handles the token's chunks
+// threadIdx.x, threadIdx.x + 128, ..., all at chunk position c16 =
+// threadIdx.x mod 16 of their head, so its 4 RoPE table entries are looked up
+// once per token.
+__global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
+  const int nch = p.H * 16;
+  const int c16 = threadIdx.x & 15;
+  const long long eoff = (long long)c16 * 8;
+  for (int s = blockIdx.x; s < p.Ls; s += gridDim.x) {
     const int t = p.rank * p.Ls + s;
-    const long long eoff = (long long)c16 * 8;
-    const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + 2 * (s * p.q_sl + h * p.q_sh + eoff)));
-    uint4 kv = __ldg(reinterpret_cast<const uint4*>(p.k + 2 * (s * p.k_sl + h * p.k_sh + eoff)));
-    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(p.v + 2 * (s * p.v_sl + h * p.v_sh + eoff)));
-    if (p.rope_on) kv = rope_chunk(kv, c16, rope_token(p.rope, t, 0));
-    const long long qoff = 2 * (((long long)t * p.Hp + hl) * 128 + eoff);
-    const long long coff = 2 * (((long long)(p.dst_start + t) * p.Hp + hl) * 128 + eoff);
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.q_dst[owner]) + qoff) = qv;
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ck_dst[owner]) + coff) = kv;
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv;
+    double2 cs[4];
+    float2 dl[4];
+    bool rot = false, has_d = false;
+    if (p.rope_on) {
+      const RopeToken rt = rope_token(p.rope, t, 0);
+      rot = rt.on;
+      has_d = rt.dl != nullptr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        cs[j] = rope_freq(4 * c16 + j, rt);
+        dl[j] = has_d ? rt.dl[4 * c16 + j] : make_float2(0.f, 0.f);
+      }
+    }
+    for (int c = threadIdx.x; c < nch; c += SCATTER_THREADS) {
+      const int h = c >> 4;
+      const int owner = h / p.Hp, hl = h - owner * p.Hp;
+      const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + 2 * (s * p.q_sl + h * p.q_sh + eoff)));
+      uint4 kv = __ldg(reinterpret_cast<const uint4*>(p.k + 2 * (s * p.k_sl + h * p.k_sh + eoff)));
+      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(p.v + 2 * (s * p.v_sl + h * p.v_sh + eoff)));
+      if (rot) {
+        kv.x = rope_rotate(kv.x, cs[0], has_d, dl[0]);
+        kv.y = rope_rotate(kv.y, cs[1], has_d, dl[1]);
+        kv.z = rope_rotate(kv.z, cs[2], has_d, dl[2]);
+        kv.w = rope_rotate(kv.w, cs[3], has_d, dl[3]);
+      }
+      const long long qoff = 2 * (((long long)t * p.Hp + hl) * 128 + eoff);
+      const long long coff = 2 * (((long long)(p.dst_start + t) * p.Hp + hl) * 128 + eoff);
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.q_dst[owner]) + qoff) = qv;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ck_dst[owner]) + coff) = kv;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv;
+    }
   }
 }
 
@@ -156,7 +179,13 @@ extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, lo
     p.rope = *rope;
     p.rope_on = 1;
   }
-  sp::scatter_qkv_kernel<<<sp::grid_for((long long)Ls * H * 16), 256, 0, (cudaStream_t)stream>>>(p);
+  {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = Ls < sms * 16 ? Ls : sms * 16;
+    sp::scatter_qkv_kernel<<<grid, sp::SCATTER_THREADS, 0, (cudaStream_t)stream>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
 

@@ -1,6 +1,8 @@
 """RoPE + cache store, landmark gather (bulk copies), bank decisions and the
 Ulysses layout transforms on the GPU, against the oracle and the reference's
 fixtures.  Integer / byte / index results are compared bit for bit."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -238,3 +240,53 @@ def test_sp_barrier_single_rank_and_timeout(cuda):
     assert lib.rw_sp_barrier(ctypes.c_void_p(ptrs.data_ptr()), 0, 3, 5, 1, 100, None, stream) == -1   # rank >= P
     x = torch.ones(16, device=cuda)
     assert float((x * 2).sum()) == 32.0                      # context still usable
+
+
+@pytest.mark.parametrize("P,rank", [(1, 0), (2, 1), (4, 2)])
+def test_sp_scatter_qkv_emulated_ranks(cuda, P, rank):
+    """rw_sp_scatter_qkv of rank `rank` of P on one GPU: the P owners' buffers are
+    local tensors (the kernel only stores through its pointer arrays and waits on
+    nothing).  q rows, v cache rows and RoPE(+PM-RoPE) k cache rows land at the
+    owner's local head, bit-exact against the oracle."""
+    from reworld_b200 import RopeArgs, _native, device_table
+    from reworld_b200._native import c_vp
+    f, h, w = 3, 4, 5
+    ct = f * h * w + 4                       # 4 tokens past the grid stay unroped
+    H, Ls = 8, ct // P
+    Hp = H // P
+    gen = torch.Generator().manual_seed(70 + P)
+    q, k, v = ((torch.randn(Ls, H, 128, generator=gen) * 2).to(torch.bfloat16) for _ in range(3))
+    delta = torch.randn(1, f, 64, generator=gen) * 0.4
+    freqs = orope.build_freqs(128, gi.ROPE_SCALE_H, gi.ROPE_SCALE_W)
+    cap, d0 = 2 * ct, 10
+    qd = [torch.zeros(P * Ls, Hp, 128, dtype=torch.bfloat16, device=cuda) for _ in range(P)]
+    ckd = [torch.zeros(cap, Hp, 128, dtype=torch.bfloat16, device=cuda) for _ in range(P)]
+    cvd = [torch.zeros(cap, Hp, 128, dtype=torch.bfloat16, device=cuda) for _ in range(P)]
+    ptrs = [torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=cuda) for ts in (qd, ckd, cvd)]
+    rope = RopeArgs(device_table(freqs, cuda), (f, h, w), 9, delta=delta.to(cuda))
+    rs = rope.struct()
+    qg, kg, vg = q.to(cuda), k.to(cuda), v.to(cuda)
+    code = _native.lib().rw_sp_scatter_qkv(
+        c_vp(qg.data_ptr()), c_vp(kg.data_ptr()), c_vp(vg.data_ptr()), qg.stride(0), qg.stride(1),
+        kg.stride(0), kg.stride(1), vg.stride(0), vg.stride(1), *(c_vp(t.data_ptr()) for t in ptrs),
+        Ls, H, 128, P, rank, d0, cap, ctypes.byref(rs), _native.stream_ptr(cuda))
+    _native.check(code, "rw_sp_scatter_qkv")
+    torch.cuda.synchronize()
+    # the oracle's roped k for this rank's tokens (chunk positions rank * Ls + s)
+    kfull = torch.zeros(1, ct, H, 128, dtype=torch.bfloat16)
+    kfull[0, rank * Ls:(rank + 1) * Ls] = k
+    kr = orope.causal_rope_apply(kfull.float().numpy(), [(f, h, w)], freqs, start_frame=9)
+    cs = rope.delta_cs.cpu()                                                   # [1, f, 64, 2]
+    tok = cs.unsqueeze(2).expand(-1, -1, h * w, -1, -1).reshape(1, f * h * w, 1, 64, 2)
+    tok = torch.cat([tok, torch.zeros(1, ct - f * h * w, 1, 64, 2)], dim=1).numpy()
+    kr = orope.pm_rope_apply_cs(kr, tok[..., 0], tok[..., 1])
+    kr[:, f * h * w:] = kfull.float().numpy()[:, f * h * w:]
+    want_k = f32_to_bf16_bits(kr)[0, rank * Ls:(rank + 1) * Ls]              # [Ls, H, 128]
+    t0, t1 = rank * Ls, (rank + 1) * Ls
+    for p in range(P):
+        hs = slice(p * Hp, (p + 1) * Hp)
+        assert torch.equal(qd[p][t0:t1].cpu(), q[:, hs])
+        assert torch.equal(cvd[p][d0 + t0:d0 + t1].cpu(), v[:, hs])
+        assert np.array_equal(torch_bf16_to_bits(ckd[p][d0 + t0:d0 + t1]), want_k[:, hs])
+        assert not qd[p][:t0].any() and not qd[p][t1:].any()
+        assert not ckd[p][:d0 + t0].any() and not ckd[p][d0 + t1:].any()
