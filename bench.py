@@ -447,6 +447,7 @@ def gpu_side_baselines(ro, dev):
     nbytes = 2 * 2 * N_LAYERS * (N_SINK + RECENT_W + len(R)) * CT * ro.H * HEAD_DIM * 2   # read + write, k + v
     out["gather_ms"] = round(msg, 3)
     out["gather_gbs"] = round(nbytes / (msg * 1e-3) / 1e9, 1)
+    out["rope_kv_store"] = store_measure(ro, dev, timeit)
     out["qkv_norm_rope_store"] = qkv_norm_measure(ro, dev, timeit)
     out["se3_block_apply"] = se3_measure(ro, dev, timeit)
     out["host_tier"] = host_tier_measure(dev)
@@ -544,6 +545,22 @@ def _graph(dev, fn, n):
         for i in range(n):
             fn(i)
     return gr
+
+
+def store_measure(ro, dev, timeit, n_rot=8):
+    """rw_rope_kv_store as the chunk step runs it (RoPE of k, cache write of k and v
+    for one layer's chunk), launches rotating over n_rot layers' k/v and caches
+    (more than L2), timed from CUDA-graph replays."""
+    from reworld_b200 import rope_kv_store
+    rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), 0)
+    g = _graph(dev, lambda i: rope_kv_store(ro.k[i], ro.v[i], ro.cache_k[i], ro.cache_v[i], ro.tot, rope=rope),
+               n_rot)
+    ms = timeit(g.replay, n=8) / n_rot
+    nbytes = 4 * CT * HEADS * HEAD_DIM * 2          # k and v read, both cache rows written
+    _, _, hbm, peak_src = load_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"ms": round(ms, 4), "gbs": round(gbs, 1), "bytes_per_launch": nbytes, "frac_of_hbm": round(gbs / hbm, 4),
+            "peak_kind": f"copy bandwidth ({peak_src})", "timing": "CUDA graph replay, per launch"}
 
 
 def se3_measure(ro, dev, timeit, n_rot=8):
