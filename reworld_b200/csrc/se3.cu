@@ -11,8 +11,9 @@
 // bf16 matmul with fp32 accumulation rounds it; only the order of the 4-term sum
 // can differ from the library's.
 //
-// CTAs of 128 threads walk the tokens (the token's frame matrix is loaded once);
-// a thread transforms 16-byte chunks (two groups of 4).  HBM-bound: 2 bytes read
+// CTAs of 64 threads walk the tokens (the token's frame matrix is loaded once);
+// a thread transforms 16-byte chunks (two groups of 4), their loads issued
+// together.  HBM-bound: 2 bytes read
 // and 2 bytes written per element.
 #include "common.cuh"
 #include "host_util.h"
@@ -44,7 +45,9 @@ __device__ __forceinline__ void apply_group(const float (&m)[16], uint32_t a, ui
   yb = pack_bf16x2(y[2], y[3]);
 }
 
-__global__ void __launch_bounds__(128) se3_kernel(const __grid_constant__ Params p) {
+constexpr int THREADS = 64;  // small CTAs, one per token; a thread's 6 chunks (24 heads) unrolled
+
+__global__ void __launch_bounds__(THREADS) se3_kernel(const __grid_constant__ Params p) {
   const long long tokens = (long long)p.B * p.L;
   const int nch = p.H * 16;  // 16-byte chunks per token
   for (long long tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
@@ -63,7 +66,8 @@ __global__ void __launch_bounds__(128) se3_kernel(const __grid_constant__ Params
     }
     const uint8_t* xr = p.x + 2 * ((long long)b * p.x_sb + (long long)t * p.x_sl);
     uint8_t* orow = p.out + 2 * ((long long)b * p.o_sb + (long long)t * p.o_sl);
-    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+#pragma unroll 6
+    for (int c = threadIdx.x; c < nch; c += THREADS) {
       const long long h = c >> 4, e = (long long)(c & 15) * 8;
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + 2 * (h * p.x_sh + e)));
       uint4 o;
@@ -111,8 +115,8 @@ extern "C" int rw_se3_block_apply(const void* x, void* out, const float* mats, i
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long tokens = (long long)B * L;
-  const long long cap = (long long)sms * 16;  // 16 resident 128-thread CTAs per SM, tokens strided over them
+  const long long cap = (long long)sms * 20;  // tokens strided over at most 20 CTAs per SM
   const long long grid = tokens < cap ? tokens : cap;
-  se3::se3_kernel<<<(unsigned)grid, 128, 0, (cudaStream_t)stream>>>(p);
+  se3::se3_kernel<<<(unsigned)grid, se3::THREADS, 0, (cudaStream_t)stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
