@@ -42,14 +42,20 @@ def row_norm(x, weight=None, bias=None, eps=1e-6, mode="layer", out=None):
     if out is None:
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
     o2 = out.view(-1, C)
-    w = weight.detach().to(torch.bfloat16).contiguous() if weight is not None else None
-    b = bias.detach().to(torch.bfloat16).contiguous() if bias is not None else None
+    if not _bf16_or_none(weight, bias):
+        raise ValueError("row_norm weights must be bf16 (the module's dtype)")
+    w = weight.detach().contiguous() if weight is not None else None
+    b = bias.detach().contiguous() if bias is not None else None
     code = _native.lib().rw_row_norm(
         c_vp(x2.data_ptr()), c_vp(o2.data_ptr()), c_vp(w.data_ptr()) if w is not None else None,
         c_vp(b.data_ptr()) if b is not None else None, x2.shape[0], C, x2.stride(0), o2.stride(0), float(eps),
         RW_NORM_RMS if mode == "rms" else RW_NORM_LAYER, _native.stream_ptr(x.device))
     _native.check(code, "rw_row_norm")
     return out
+
+
+def _bf16_or_none(*ts):
+    return all(t is None or t.dtype == torch.bfloat16 for t in ts)
 
 
 class RowLayerNorm(nn.Module):
@@ -61,8 +67,8 @@ class RowLayerNorm(nn.Module):
 
     def forward(self, x):
         ln = self.inner
-        if x.dtype != torch.bfloat16 or not x.is_cuda:
-            return ln(x)
+        if x.dtype != torch.bfloat16 or not x.is_cuda or not _bf16_or_none(ln.weight, ln.bias):
+            return ln(x)   # outside the kernel's domain: the module's own computation
         return row_norm(x, ln.weight, ln.bias, ln.eps, "layer")
 
 
@@ -77,7 +83,8 @@ class GeluFFN(nn.Module):
 
     def forward(self, x):
         lin1, act, lin2 = self.inner[0], self.inner[1], self.inner[2]
-        if x.dtype != torch.bfloat16 or not x.is_cuda or getattr(act, "approximate", "none") != "tanh":
+        if x.dtype != torch.bfloat16 or not x.is_cuda or getattr(act, "approximate", "none") != "tanh" or \
+                not _bf16_or_none(lin1.weight, lin1.bias, lin2.weight, lin2.bias):
             return self.inner(x)
         x2 = x.reshape(-1, x.shape[-1])
         h = torch._addmm_activation(lin1.bias, x2, lin1.weight.t(), use_gelu=True)
@@ -99,7 +106,9 @@ def cross_attn_forward(self, x, context, context_lens, is_teacher_forcing=False,
     fused = x.dtype == torch.bfloat16 and x.is_cuda and self.q.weight.dtype == torch.bfloat16
 
     def norm(t, mod):
-        if fused and isinstance(mod, nn.Module) and hasattr(mod, "weight") and hasattr(mod, "eps"):
+        # WanRMSNorm with a bf16 weight on the kernel (an fp32 weight makes the
+        # reference's product fp32: the module's own computation then)
+        if fused and hasattr(mod, "weight") and hasattr(mod, "eps") and _bf16_or_none(mod.weight):
             return row_norm(t, mod.weight, None, mod.eps, "rms")
         return mod(t)
 
