@@ -15,8 +15,8 @@ model.py:162-197) and ffn Linear(dim, ffn_dim) -> GELU(tanh) -> Linear(ffn_dim, 
 cuBLASLt's epilogue, then the second GEMM) and cross_attn.forward for
 `cross_attn_forward` (norm_q / norm_k on rw_row_norm, the attention on the
 package's kernel with k_lens).  The modulation and the residual adds stay the
-reference's own elementwise ops.  bf16 modules only; other dtypes keep the
-original modules.
+reference's own elementwise ops.  CUDA tensors only; bf16 modules run the
+kernels, modules in other dtypes keep their own computation.
 """
 import types
 
@@ -67,7 +67,9 @@ class RowLayerNorm(nn.Module):
 
     def forward(self, x):
         ln = self.inner
-        if x.dtype != torch.bfloat16 or not x.is_cuda or not _bf16_or_none(ln.weight, ln.bias):
+        if not x.is_cuda:
+            raise ValueError("RowLayerNorm runs on CUDA tensors (no CPU path)")
+        if x.dtype != torch.bfloat16 or not _bf16_or_none(ln.weight, ln.bias):
             return ln(x)   # outside the kernel's domain: the module's own computation
         return row_norm(x, ln.weight, ln.bias, ln.eps, "layer")
 
@@ -83,7 +85,9 @@ class GeluFFN(nn.Module):
 
     def forward(self, x):
         lin1, act, lin2 = self.inner[0], self.inner[1], self.inner[2]
-        if x.dtype != torch.bfloat16 or not x.is_cuda or getattr(act, "approximate", "none") != "tanh" or \
+        if not x.is_cuda:
+            raise ValueError("GeluFFN runs on CUDA tensors (no CPU path)")
+        if x.dtype != torch.bfloat16 or getattr(act, "approximate", "none") != "tanh" or \
                 not _bf16_or_none(lin1.weight, lin1.bias, lin2.weight, lin2.bias):
             return self.inner(x)
         x2 = x.reshape(-1, x.shape[-1])

@@ -1,0 +1,86 @@
+"""Host-side logic of the drop-ins that needs no GPU: the stacked-weight
+bookkeeping of the self-attention, the SE3 frame matrices, the block's module
+swaps (and that they refuse CPU tensors)."""
+import pytest
+import torch
+import torch.nn as nn
+
+import inputs as gi
+from oracle import self_attn as osa
+
+
+class _Lin3(nn.Module):
+    def __init__(self, dim):
+        super().__init__()
+        self.q, self.k, self.v = (nn.Linear(dim, dim) for _ in range(3))
+        self.o, self.prope_proj = nn.Linear(dim, dim), nn.Linear(dim, dim)
+
+
+def test_stacked_qkv_views_keep_values_and_follow_replacement():
+    from reworld_b200.self_attn import _stacked_out, _stacked_qkv
+    torch.manual_seed(0)
+    m = _Lin3(64)
+    before = {n: p.detach().clone() for n, p in m.named_parameters()}
+    W, b = _stacked_qkv(m)
+    assert W.shape == (192, 64) and b.shape == (192,)
+    for i, lin in enumerate((m.q, m.k, m.v)):
+        assert lin.weight.data_ptr() == W[64 * i].data_ptr()          # a view, no second copy
+    for n, p in m.named_parameters():
+        assert torch.equal(p, before[n]), n
+    x = torch.randn(3, 64)
+    assert torch.equal(nn.functional.linear(x, W, b)[:, 64:128], m.k(x))
+    # in-place updates reach the stacked buffer; a replaced parameter triggers a rebuild
+    with torch.no_grad():
+        m.v.weight.add_(1.0)
+    assert torch.equal(_stacked_qkv(m)[0][128:], m.v.weight)
+    m.k.weight.data = torch.zeros(64, 64)
+    W2, _ = _stacked_qkv(m)
+    assert not W2[64:128].any() and m.k.weight.data_ptr() == W2[64].data_ptr()
+    Wo, bo = _stacked_out(m)
+    assert Wo.shape == (64, 128) and torch.equal(bo, m.o.bias + m.prope_proj.bias)
+    y = torch.randn(3, 128)
+    ref = m.o(y[:, :64]) + m.prope_proj(y[:, 64:])
+    assert torch.allclose(nn.functional.linear(y, Wo, bo), ref, atol=1e-5)
+
+
+@pytest.mark.parametrize("mode", ["P", "P_inv"])
+def test_se3_mats_match_oracle(mode):
+    from reworld_b200.self_attn import se3_mats
+    torch.manual_seed(1)
+    ctx = torch.eye(4).repeat(1, 5, 1, 1)
+    ctx[..., :3, :3] = torch.linalg.qr(torch.randn(1, 5, 3, 3))[0]
+    ctx[..., :3, 3] = torch.randn(1, 5, 3)
+    got = se3_mats(ctx, mode, 3, torch.bfloat16)
+    c = ctx[:, -3:].to(torch.bfloat16)
+    want = (osa._inv_se3(c) if mode == "P_inv" else c).float()
+    assert got.dtype == torch.float32 and got.is_contiguous() and torch.equal(got, want)
+
+
+def test_block_install_swaps_modules_and_refuses_cpu_tensors():
+    from reworld_b200 import block as rb
+
+    class Blk(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.norm3 = nn.LayerNorm(gi.BLOCK_DIM, 1e-6, elementwise_affine=True)
+            self.norm2 = nn.LayerNorm(gi.BLOCK_DIM, 1e-6, elementwise_affine=False)
+            self.ffn = nn.Sequential(nn.Linear(gi.BLOCK_DIM, 32), nn.GELU(approximate="tanh"),
+                                     nn.Linear(32, gi.BLOCK_DIM))
+            self.cross_attn = nn.Module()
+            self.cross_attn.forward = lambda *a, **k: None
+
+    blk = Blk()
+    ln3 = blk.norm3
+    assert rb.install([blk]) == 1
+    assert isinstance(blk.norm3, rb.RowLayerNorm) and blk.norm3.inner is ln3
+    assert isinstance(blk.norm2, rb.RowLayerNorm) and isinstance(blk.ffn, rb.GeluFFN)
+    assert hasattr(blk.cross_attn, "_rw_reference_forward")
+    rb.install([blk])                                   # idempotent: no double wrapping
+    assert isinstance(blk.norm2.inner, nn.LayerNorm) and not isinstance(blk.norm2.inner, rb.RowLayerNorm)
+    x = torch.randn(1, 4, gi.BLOCK_DIM)
+    with pytest.raises(ValueError):
+        blk.norm2(x)
+    with pytest.raises(ValueError):
+        blk.ffn(x)
+    with pytest.raises(ValueError):
+        rb.row_norm(x.bfloat16())
