@@ -290,3 +290,33 @@ def test_sp_scatter_qkv_emulated_ranks(cuda, P, rank):
         assert np.array_equal(torch_bf16_to_bits(ckd[p][d0 + t0:d0 + t1]), want_k[:, hs])
         assert not qd[p][:t0].any() and not qd[p][t1:].any()
         assert not ckd[p][:d0 + t0].any() and not ckd[p][d0 + t1:].any()
+
+
+def test_rope_store_two_batches_with_q_and_phase(cuda):
+    """B = 2 with a per-batch PM-RoPE phase and the optional roped q copy: every
+    row bit-exact against the oracle (the kernel walks tokens of both batches)."""
+    from reworld_b200 import RopeArgs, device_table, rope_kv_store
+    gen = torch.Generator().manual_seed(81)
+    f, h, w, H = 3, 4, 5, 3
+    B, L = 2, f * h * w + 4
+    k, v, q = ((torch.randn(B, L, H, 128, generator=gen) * 2).to(torch.bfloat16) for _ in range(3))
+    delta = torch.randn(B, f, 64, generator=gen) * 0.4
+    freqs = orope.build_freqs(128, gi.ROPE_SCALE_H, gi.ROPE_SCALE_W)
+    ck = torch.zeros(B, L + 9, H, 128, dtype=torch.bfloat16, device=cuda)
+    cv = torch.zeros_like(ck)
+    rope = RopeArgs(device_table(freqs, cuda), (f, h, w), 5, delta=delta.to(cuda))
+    q_out = rope_kv_store(k.to(cuda), v.to(cuda), ck, cv, 9, rope=rope, q=q.to(cuda))
+    torch.cuda.synchronize()
+    cs = rope.delta_cs.cpu()
+    tok = cs.unsqueeze(2).expand(-1, -1, h * w, -1, -1).reshape(B, f * h * w, 1, 64, 2)
+    tok = torch.cat([tok, torch.zeros(B, L - f * h * w, 1, 64, 2)], dim=1).numpy()
+
+    def want(x):
+        y = orope.causal_rope_apply(x.float().numpy(), [(f, h, w)] * B, freqs, start_frame=5)
+        y = orope.pm_rope_apply_cs(y, tok[..., 0], tok[..., 1])
+        y[:, f * h * w:] = x.float().numpy()[:, f * h * w:]
+        return f32_to_bf16_bits(y)
+
+    assert np.array_equal(torch_bf16_to_bits(ck[:, 9:]), want(k))
+    assert np.array_equal(torch_bf16_to_bits(q_out), want(q))
+    assert torch.equal(cv[:, 9:].cpu(), v) and not ck[:, :9].any() and not cv[:, :9].any()

@@ -99,3 +99,19 @@ def test_se3_rejects_partial_frames(cuda):
         se3_block_apply(x, ctx, "P", 20)
     with pytest.raises(ValueError):
         se3_block_apply(x.float(), ctx, "P", 25)
+
+
+def test_se3_kernel_two_batches(cuda):
+    """B = 2, each batch with its own frames' matrices, against the oracle."""
+    gen = torch.Generator().manual_seed(17)
+    B, H, fs, nf = 2, 3, 20, 3
+    L = nf * fs
+    x = (torch.randn(B, L, H, 128, generator=gen) * 1.5).to(torch.bfloat16)
+    ctx = _poses(B, nf, gen)
+    want = osa._se3(x, ctx, "P", fs)
+    mats = ctx.to(torch.bfloat16).float().contiguous()
+    out = torch.empty(B, L, H, 128, dtype=torch.bfloat16, device=cuda)
+    _raw(x.to(cuda), out, mats.to(cuda), fs)
+    torch.cuda.synchronize()
+    u = _ulps(out.cpu(), want.contiguous())
+    assert u.max() <= 1 and (u == 0).mean() > 0.99, (u.max(), (u == 0).mean())

@@ -157,3 +157,24 @@ def test_rejects_mismatched_shapes(cuda):
         qkv_norm_rope_store(x, x, x, w.float(), w, ck, ck.clone(), 0, 1e-6)   # fp32 norm weight
     with pytest.raises(ValueError):
         qkv_norm_rope_store(x, x, x[..., :128], w, w, ck, ck.clone(), 0, 1e-6)
+
+
+def test_width_of_the_14b_model(cuda):
+    """40 heads (C = 5120: 7 token slots per CTA instead of 10), B = 2, against the
+    oracle's norm; v rows exact."""
+    from reworld_b200 import qkv_norm_rope_store
+    gen = torch.Generator().manual_seed(91)
+    B, L, H = 2, 300, 40
+    C = H * 128
+    q, k, v = ((torch.randn(B, L, C, generator=gen) * 2).to(torch.bfloat16) for _ in range(3))
+    wq, wk = ((1 + 0.05 * torch.randn(C, generator=gen)).to(torch.bfloat16) for _ in range(2))
+    _, qr, kr, vr = _rows(q.to(cuda), k.to(cuda), v.to(cuda))
+    ck = torch.zeros(B, L + 4, H, 128, dtype=torch.bfloat16, device=cuda)
+    cv = torch.zeros_like(ck)
+    q_out = qkv_norm_rope_store(qr, kr, vr, wq.to(cuda), wk.to(cuda), ck, cv, 4, 1e-6)
+    torch.cuda.synchronize()
+    for got, x, wt in ((q_out, q, wq), (ck[:, 4:], k, wk)):
+        u = _ulps(got.cpu(), osa.rms_norm(x, wt, 1e-6).view(B, L, H, 128))
+        assert u.max() <= 2 and (u == 0).mean() > 0.99, (u.max(), (u == 0).mean())
+    assert torch.equal(cv[:, 4:].cpu(), v.view(B, L, H, 128))
+    _status_clean()
