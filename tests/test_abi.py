@@ -115,3 +115,16 @@ def test_attn_workspace_plan():
     n = lib.rw_attn_workspace_bytes(1, 2640, 34320, 24)
     assert n > 0 and n % (4 * (128 * 256 + 512)) == 0
     assert lib.rw_attn_workspace_bytes(0, 1, 1, 1) == 0
+
+
+def test_ctypes_bindings_match_header_parameter_counts():
+    """Every declaration in include/reworld_b200.h has as many parameters as the
+    ctypes binding of the same name (a mismatch would shift every later argument)."""
+    src = open(os.path.join(ROOT, "include", "reworld_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = dict(re.findall(r"\b(rw_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src))
+    assert set(decls) == set(_native.exported_symbols())
+    for name, params in decls.items():
+        params = params.strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert n == len(_native._SIGNATURES[name][1]), (name, n, len(_native._SIGNATURES[name][1]))
