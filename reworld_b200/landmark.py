@@ -26,6 +26,7 @@ import collections
 import ctypes
 import math
 import os
+import warnings
 
 import numpy as np
 import torch
@@ -186,6 +187,35 @@ def copy_jobs(jobs, device, status=None):
     # reused before the copy kernel (queued earlier on the same stream) has read it.
 
 
+def _available_ram():
+    try:
+        import psutil
+        return psutil.virtual_memory().available
+    except Exception:  # noqa: BLE001 - no psutil / no /proc: no cap
+        return None
+
+
+def host_pool(n_slots, member_shape, dtype):
+    """Pinned host pool [n, *member_shape] for the tiered bank, sized as the
+    reference sizes its host tier (landmark_cache_v2.py:176-203): at most half of
+    the free RAM, and halved while a pinned allocation fails.  The returned pool's
+    length is the bank capacity that fits (the caller lowers K to it)."""
+    member_bytes = int(np.prod(member_shape)) * torch.empty((), dtype=dtype).element_size()
+    n = int(n_slots)
+    avail = _available_ram()
+    if avail is not None and member_bytes * n > 0.5 * avail:
+        n = max(1, int((0.5 * avail) // max(member_bytes, 1)))
+        warnings.warn(f"[tiered-store] host pool capped by free RAM: {n_slots} -> {n} slots")
+    while True:
+        try:
+            return torch.empty((n,) + tuple(member_shape), dtype=dtype, pin_memory=True)
+        except RuntimeError:
+            if n <= 1:
+                raise
+            n //= 2
+            warnings.warn(f"[tiered-store] pinned alloc failed, retry with {n} slots")
+
+
 class _HostTier:
     """Pinned host master copies of the bank members and the device hot set.
 
@@ -202,10 +232,10 @@ class _HostTier:
 
     def __init__(self, n_slots, pool, hot_capacity):
         member = tuple(pool.pool.shape[1:])
-        self.host = torch.empty((n_slots,) + member, dtype=pool.pool.dtype, pin_memory=True)
+        self.host = host_pool(n_slots, member, pool.pool.dtype)
         self.pool = pool
         self.hot_capacity = hot_capacity
-        self.free = collections.deque(range(n_slots))
+        self.free = collections.deque(range(self.host.shape[0]))
         self.m2s = {}                          # member id -> host slot
         self.slot_ev = {}                      # host slot -> last transfer event touching it
         self.master_ev = {}                    # member id -> write-through event
@@ -369,6 +399,8 @@ class LandmarkBankStack:
         self.pool = _ChunkPool(n_dev, n_layers, chunk_tokens, num_heads, head_dim, self.device, dtype)
         if host_tier:
             self.tier = _HostTier(K, self.pool, hot)
+            if self.tier.host.shape[0] < K:   # the host pool was capped: keep the capacity honest
+                K = self.K = self.tier.host.shape[0]
         self.dec = DeviceBankDecisions(K, retrieve_k, mode, protect_n, self.device)
         self.sink, self.recent, self.bank = [], [], []
         self.events = []
@@ -516,6 +548,7 @@ class LandmarkCacheV2:
                                             host_tier=self.host_tier, hot_gpu=self.hot_gpu,
                                             gpu_spare=self.gpu_spare)
             self._stack.events = self.events
+            self.K = self._stack.K             # lowered when the host pool was capped
 
     @property
     def sink(self):

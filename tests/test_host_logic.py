@@ -84,3 +84,35 @@ def test_block_install_swaps_modules_and_refuses_cpu_tensors():
         blk.ffn(x)
     with pytest.raises(ValueError):
         rb.row_norm(x.bfloat16())
+
+
+def test_host_pool_capped_by_ram_and_halved_on_failed_pinning(monkeypatch):
+    """The tiered bank's pinned pool follows the reference's sizing: at most half of
+    the free RAM, halved while pinning fails (the bank's K is lowered to fit)."""
+    import warnings as _w
+    from reworld_b200 import landmark as lm
+    real_empty = torch.empty
+    calls = []
+
+    def fake_empty(*shape, pin_memory=False, **kw):
+        dims = shape[0] if len(shape) == 1 and isinstance(shape[0], tuple) else shape
+        n = dims[0] if len(dims) else 0
+        calls.append(n)
+        if pin_memory and n > 3:
+            raise RuntimeError("cannot pin that much")
+        return real_empty(*shape, **kw)
+
+    monkeypatch.setattr(lm, "_available_ram", lambda: None)
+    monkeypatch.setattr(lm.torch, "empty", fake_empty)
+    with _w.catch_warnings(record=True) as rec:
+        _w.simplefilter("always")
+        pool = lm.host_pool(16, (2, 4, 8), torch.bfloat16)
+    assert pool.shape == (2, 2, 4, 8) and [c for c in calls if c] == [16, 8, 4, 2]
+    assert any("retry with" in str(r.message) for r in rec)
+    # free-RAM cap: half of what is available
+    member = 2 * 4 * 8 * 2
+    monkeypatch.setattr(lm, "_available_ram", lambda: 2 * 3 * member + 1)
+    with _w.catch_warnings(record=True) as rec:
+        _w.simplefilter("always")
+        pool = lm.host_pool(16, (2, 4, 8), torch.bfloat16)
+    assert pool.shape[0] == 3 and any("capped by free RAM" in str(r.message) for r in rec)
