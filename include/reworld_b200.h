@@ -86,11 +86,15 @@ long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H);
  * streaming loop where a cudaMalloc (which can synchronise the whole device)
  * would stall frame delivery.  Same arguments as rw_attn_fwd without the
  * workspace: the key-split scratch is a fixed array inside the library, of
- * RW_ATTN_NOALLOC_SCRATCH_BYTES (80 MiB; the 704x1280 chunk shape needs about
- * 74 MiB) of device memory that each GPU loading it keeps until the process
- * exits.  Shapes whose scratch (rw_attn_workspace_bytes) exceeds it return
- * RW_ERR_CAPACITY.  The first call on a device looks the array's device address
- * up (once per device); make that first call before any stream capture.  All
+ * RW_ATTN_NOALLOC_SCRATCH_BYTES (80 MiB) of device memory that each GPU loading
+ * it keeps until the process exits.  A call needs 0 bytes or 2 x 133,120 bytes
+ * per resident pair, whatever the shape: 19.7 MB with the 74 pairs of a B200
+ * (the 704x1280 chunk included), so only a device with more than 315 resident
+ * pairs could exceed the array; shapes whose scratch (rw_attn_workspace_bytes)
+ * exceeds it return RW_ERR_CAPACITY.  `stream` must belong to the current
+ * device (RW_ERR_INVALID_ARG otherwise).  The first call on a device looks the
+ * array's device address up (once per device); make that first call before any
+ * stream capture.  All
  * calls share the array, so calls that overlap on the GPU race; nothing in it
  * needs clearing between calls.  No counterpart in the reference: it is an
  * allocation-free form of this library's own entry point. */

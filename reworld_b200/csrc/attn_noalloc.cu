@@ -10,8 +10,12 @@
 // compiled into the library, so it allocates nothing.
 //
 // The array is RW_ATTN_NOALLOC_SCRATCH_BYTES (80 MiB) of device memory that every
-// GPU loading this part of the library holds until the process exits.  Shapes
-// whose split would need more are refused with RW_ERR_CAPACITY.  All calls share
+// GPU loading this part of the library holds until the process exits.  The split
+// needs 2 partial-result slots of 133,120 bytes per resident pair, whatever the
+// shape: 19.7 MB with the 74 pairs of a B200, so the array is exceeded only on a
+// device with more than 315 resident pairs; such shapes are refused with
+// RW_ERR_CAPACITY.  The stream must belong to the current device (the array's
+// address is per device); another device's stream is refused.  All calls share
 // the one array: calls that overlap on the GPU (other streams, other host
 // threads) race on it.  Nothing in it has to start at zero: every partial slot
 // the merge step reads is written earlier in the same call.
@@ -51,6 +55,12 @@ extern "C" int rw_attn_fwd_noalloc(const void* q, const void* k, const void* v, 
                                    long long k_sl, long long k_sh, long long v_sb, long long v_sl, long long v_sh,
                                    long long o_sb, long long o_sl, long long o_sh, float softmax_scale,
                                    const rw_rope_t* rope, int* status, void* stream) {
+  if (stream != nullptr) {
+    int cur = -1, sdev = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cudaStreamGetDevice((cudaStream_t)stream, &sdev) != cudaSuccess)
+      return RW_ERR_CUDA;
+    if (sdev != cur) return RW_ERR_INVALID_ARG;
+  }
   const long long need = rw_attn_workspace_bytes(B, Lq, Lk, H);
   if (need > RW_ATTN_NOALLOC_SCRATCH_BYTES) return RW_ERR_CAPACITY;
   void* scratch = nullptr;

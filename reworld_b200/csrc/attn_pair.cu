@@ -702,11 +702,14 @@ namespace rw {
 namespace pair {
 
 // Pairs that can be resident at once (cluster placement may leave SMs unused).
+// Cached per device; concurrent first calls from several host threads compute
+// the same value and the atomic store keeps the cache well defined.
 int resident_pairs() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 74;
-  if (cached[dev] > 0) return cached[dev];
+  const int known = cached[dev].load(std::memory_order_acquire);
+  if (known > 0) return known;
   int n = 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2, 1, 1);
@@ -727,7 +730,7 @@ int resident_pairs() {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     n = sms / 2;
   }
-  cached[dev] = n;
+  cached[dev].store(n, std::memory_order_release);
   return n;
 }
 
@@ -742,7 +745,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
       make_bf16_bl_hd_map(&mv, v, B, Lk, H, HD, v_sb, v_sl, v_sh, BN) ||
       make_bf16_bl_hd_map(&mo, o, B, Lq, H, HD, o_sb, o_sl, o_sh, BM))
     return RW_ERR_DRIVER;
-  static unsigned long long attr_done = 0;
+  static std::atomic<unsigned long long> attr_done{0};
   if (!ensure_smem_attr((const void*)attn_pair_kernel, SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
   Params prm{};
   prm.B = B;

@@ -140,7 +140,7 @@ extern "C" int rw_copy_chunks(const rw_copy_desc_t* descs, int n, int* status, v
   if (n < 0) return RW_ERR_INVALID_ARG;
   if (n == 0) return RW_OK;
   if (!descs) return RW_ERR_INVALID_ARG;
-  static unsigned long long attr_done = 0;
+  static std::atomic<unsigned long long> attr_done{0};
   if (!ensure_smem_attr((const void*)copy::copy_chunks_kernel, copy::SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);

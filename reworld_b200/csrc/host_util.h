@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace rw {
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -53,13 +55,15 @@ inline int make_bf16_bl_hd_map(CUtensorMap* m, const void* ptr, int B, int L, in
 }
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
-inline bool ensure_smem_attr(const void* func, int bytes, unsigned long long* done_mask) {
+// Host threads may race here: the attribute call is idempotent and the mask is
+// atomic, so a second thread at worst repeats the call.
+inline bool ensure_smem_attr(const void* func, int bytes, std::atomic<unsigned long long>* done_mask) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   const unsigned long long bit = 1ull << dev;
-  if (*done_mask & bit) return true;
+  if (done_mask->load(std::memory_order_acquire) & bit) return true;
   if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
-  *done_mask |= bit;
+  done_mask->fetch_or(bit, std::memory_order_release);
   return true;
 }
 

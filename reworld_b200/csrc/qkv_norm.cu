@@ -356,7 +356,7 @@ extern "C" int rw_qkv_norm_rope_store(const void* q_in, const void* k_in, const 
   int slots = qkvn::STAGE_BUDGET / stage_bytes;  // one stage per token slot (warp pair)
   if (slots > qkvn::MAX_SLOTS) slots = qkvn::MAX_SLOTS;
   const int smem = slots * stage_bytes;
-  static unsigned long long attr_done = 0;
+  static std::atomic<unsigned long long> attr_done{0};
   if (!ensure_smem_attr((const void*)qkvn::qkv_norm_kernel, qkvn::STAGE_BUDGET, &attr_done)) return RW_ERR_CUDA;
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);

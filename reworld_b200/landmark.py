@@ -27,6 +27,7 @@ import ctypes
 import math
 import os
 import warnings
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -35,6 +36,68 @@ from . import _native
 from ._native import c_vp
 
 BANK_MAX = 1024
+
+
+# ---------------------------------------------------------------- rollout-side sizing and poses
+# kv_compression policies that run the landmark bank (compressed.py:302-306):
+# policy -> (mode, diverse).  'a' attends the whole bank, 'b' retrieves top-k.
+LANDMARK_POLICIES = {"consol": ("a", False), "consol_div": ("a", True), "v15a": ("a", False),
+                     "v15b": ("b", False), "v15c": ("b", True)}
+
+
+class BudgetSplit(NamedTuple):
+    """How a KV budget of `budget` chunks is spent: sink + recent + landmarks."""
+    budget: int          # effective budget (capped to what the cache holds)
+    n_sink: int
+    recent_w: int        # effective recent window
+    n_landmark: int      # landmarks attended per chunk (retrieve_k)
+    K: int               # bank capacity
+    mode: str
+    diverse: bool
+
+
+def budget_split(budget_chunks, n_sink, recent_w, landmark_k=30, policy="v15b", cache_tokens=None,
+                 chunk_tokens=None):
+    """The compressed pipeline's budget split (pipeline/
+    causal_diffusion_inference_compressed.py:273-282 and :302-322): the budget is
+    capped to the chunks the pre-allocated cache holds (cache_tokens //
+    chunk_tokens, when given); the recent window is capped so at least one
+    landmark slot survives, eff_recent = min(recent_w, max(1, B - n_sink - 1));
+    the landmarks fill the rest, n_landmark = max(1, B - n_sink - eff_recent);
+    the bank holds K = max(landmark_k, n_landmark) for the top-k policies and
+    exactly n_landmark for the attend-all ones.  Raises ValueError for a policy
+    that does not use the landmark bank."""
+    if policy not in LANDMARK_POLICIES:
+        raise ValueError(f"policy {policy!r} does not use the landmark bank (one of {sorted(LANDMARK_POLICIES)})")
+    mode, diverse = LANDMARK_POLICIES[policy]
+    budget = int(budget_chunks)
+    if cache_tokens is not None:
+        if not chunk_tokens:
+            raise ValueError("cache_tokens needs chunk_tokens")
+        budget = min(budget, int(cache_tokens) // int(chunk_tokens))
+    n_sink = int(n_sink)
+    eff_recent = min(int(recent_w), max(1, budget - n_sink - 1))
+    n_landmark = max(1, budget - n_sink - eff_recent)
+    K = max(int(landmark_k), n_landmark) if mode == "b" else n_landmark
+    return BudgetSplit(budget, n_sink, eff_recent, n_landmark, K, mode, diverse)
+
+
+def chunk_pose(prope_ctx, num_frame_per_block):
+    """One (4, 4) float32 pose for the chunk just generated, as the compressed
+    pipeline's _compute_chunk_pose forms it (causal_diffusion_inference_
+    compressed.py:355-377): the rotation of the chunk's first frame and the mean
+    translation over its frames, from the last num_frame_per_block entries of
+    prope_ctx [B, T_seen, 4, 4] (batch 0), in fp32 with numpy's reduction.  The
+    pose is host data for the bank's decision (pose_record), so the few bytes
+    are read back here as the reference reads them."""
+    if prope_ctx is None:
+        raise RuntimeError("chunk_pose: prope_context is None; the landmark bank needs the model's "
+                           "camera context (use_prope)")
+    cur = prope_ctx[0, -num_frame_per_block:].detach().to(torch.float32).cpu().numpy()
+    out = np.eye(4, dtype=np.float32)
+    out[:3, :3] = cur[0, :3, :3]
+    out[:3, 3] = cur[:, :3, 3].mean(axis=0)
+    return out
 
 
 class RwPose(ctypes.Structure):
@@ -102,8 +165,11 @@ class DeviceBankDecisions:
             recs[0] = pose_record(admit[0])
         if target is not None:
             recs[1] = pose_record(target)
-        host = torch.frombuffer(bytearray(bytes(recs)), dtype=torch.uint8)
-        self.poses.copy_(host)
+        # pinned staging: the copy is queued without a host wait; the pinned block is
+        # not reused before the copy has run (torch's pinned allocator records it)
+        host = torch.empty(len(bytes(recs)), dtype=torch.uint8, pin_memory=True)
+        host.numpy()[:] = np.frombuffer(bytes(recs), dtype=np.uint8)
+        self.poses.copy_(host, non_blocking=True)
         p0 = self.poses.data_ptr()
         ps = ctypes.sizeof(RwPose)
         lib = _native.lib()
@@ -176,8 +242,11 @@ def copy_jobs(jobs, device, status=None):
     """Runs [(src_ptr, dst_ptr, nbytes), ...] with one rw_copy_chunks launch."""
     if not jobs:
         return
-    arr = torch.tensor(np.asarray(jobs, dtype=np.int64).reshape(-1, 3), dtype=torch.int64)
-    d = arr.to(device, non_blocking=False)
+    # descriptors through pinned memory: the host-to-device copy is queued without
+    # a host wait (torch's pinned allocator keeps the block until the copy ran)
+    arr = torch.empty((len(jobs), 3), dtype=torch.int64, pin_memory=True)
+    arr.numpy()[:] = np.asarray(jobs, dtype=np.int64).reshape(-1, 3)
+    d = arr.to(device, non_blocking=True)
     st = status if status is not None else _native.status_tensor(torch.device(device))
     lib = _native.lib()
     with torch.cuda.device(device):
@@ -405,6 +474,18 @@ class LandmarkBankStack:
         self.sink, self.recent, self.bank = [], [], []
         self.events = []
         self._n = 0
+
+    @classmethod
+    def from_budget(cls, chunk_tokens, n_layers, num_heads, head_dim, budget_chunks, n_sink=1, recent_w=5,
+                    landmark_k=30, policy="v15b", cache_tokens=None, **kw):
+        """The bank the compressed pipeline builds for a KV budget (budget_split:
+        sink, effective recent window, retrieve_k = n_landmark, bank capacity K,
+        mode from the policy); `split` on the result records the split."""
+        sp = budget_split(budget_chunks, n_sink, recent_w, landmark_k, policy, cache_tokens, chunk_tokens)
+        st = cls(chunk_tokens, n_layers, num_heads, head_dim, n_sink=sp.n_sink, recent_w=sp.recent_w, K=sp.K,
+                 retrieve_k=sp.n_landmark, mode=sp.mode, **kw)
+        st.split = sp
+        return st
 
     # -- chunk admission ----------------------------------------------------
     def add_chunk_from(self, src_k, src_v, pose, pose_next=None):

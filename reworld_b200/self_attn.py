@@ -20,7 +20,9 @@ Install it per block the way the reference installs its sequence-parallel
 forward (wan_5b/text2video.py:150-154): `install(model)`.
 """
 import math
+import sys
 import types
+import weakref
 
 import torch
 
@@ -43,28 +45,47 @@ def _invert_se3(T):
     return out
 
 
-def se3_mats(prope_context, mode, n_frames, dtype):
+def _ref_flag(module_obj, name):
+    """A module-level switch of the reference model module that defines the
+    attention class (action_model.py:65-67: _PROPE_LOG_T, _SE3_T_BOUND, set by
+    CausalWanActionModel's constructor, :604-608); False when absent."""
+    mod = sys.modules.get(type(module_obj).__module__)
+    return bool(getattr(mod, name, False))
+
+
+def _bound_t(ctx):
+    """Row-wise translation bound t / (1 + |t|) of action_model.py:97-102."""
+    t = ctx[..., :3, 3]
+    ctx = ctx.clone()
+    ctx[..., :3, 3] = t / (1.0 + t.norm(dim=-1, keepdim=True))
+    return ctx
+
+
+def se3_mats(prope_context, mode, n_frames, dtype, t_bound=False):
     """The frames' 4x4 matrices as _se3_block_apply forms them (action_model.py:
-    96-104, translation bound off as by default): the last n_frames contexts cast
-    to the activation dtype, inverted in that dtype for 'P_inv'; returned as fp32
-    [B, n_frames, 4, 4] (same values) for the kernel."""
+    96-104): the last n_frames contexts cast to the activation dtype, the
+    translation bounded first when the reference's _SE3_T_BOUND switch is on,
+    inverted in that dtype for 'P_inv'; returned as fp32 [B, n_frames, 4, 4]
+    (same values) for the kernel."""
     ctx = prope_context[:, -n_frames:].to(dtype)
+    if t_bound:
+        ctx = _bound_t(ctx)
     if mode == "P_inv":
         ctx = _invert_se3(ctx)
     return ctx.float().contiguous()
 
 
-def se3_block_apply(x, prope_context, mode, frame_seqlen, out=None):
+def se3_block_apply(x, prope_context, mode, frame_seqlen, out=None, t_bound=False):
     """Block-diagonal 4x4 transform over head_dim per frame (action_model.py:84-114)
     with one rw_se3_block_apply launch.  x: bf16 [B, L, H, 128] on the GPU (any
     strides with a contiguous head dim); returns `out` (default: a new contiguous
-    [B, L, H, 128] tensor)."""
+    [B, L, H, 128] tensor).  t_bound: the reference's _SE3_T_BOUND switch."""
     B, L, H, D = x.shape
     if x.dtype != torch.bfloat16 or not x.is_cuda:
         raise ValueError("se3_block_apply runs on bf16 CUDA tensors")
     if L % frame_seqlen != 0:
         raise ValueError(f"{L} tokens are not whole frames of {frame_seqlen}")
-    mats = se3_mats(prope_context, mode, L // frame_seqlen, x.dtype).to(x.device)
+    mats = se3_mats(prope_context, mode, L // frame_seqlen, x.dtype, t_bound).to(x.device)
     if out is None:
         out = torch.empty((B, L, H, D), dtype=torch.bfloat16, device=x.device)
     lib = _native.lib()
@@ -120,17 +141,55 @@ def _stacked_out(self):
     return W, bias
 
 
+# Host mirrors of the kv_cache index tensors this module wrote last:
+# id(tensor) -> (weak reference, version counter after the write, value).  A
+# tensor's version counter advances with every in-place write, so a mirror is
+# used only while nobody else (e.g. the pipeline's local_end_index.fill_ after
+# the landmark assembly) has written the tensor since; otherwise the value is
+# read from the device.  This saves two device synchronisations per layer.
+_INDEX_MIRROR = {}
+
+
+def _version(t):
+    try:
+        return t._version
+    except RuntimeError:      # inference-mode tensors keep no version counter
+        return None
+
+
+def read_index(t):
+    """int(t.item()) for a one-element index tensor, from the host mirror when
+    this module wrote the tensor last."""
+    ent = _INDEX_MIRROR.get(id(t))
+    ver = _version(t)
+    if ent is not None and ver is not None and ent[0]() is t and ent[1] == ver:
+        return ent[2]
+    return int(t.item())
+
+
+def write_index(t, value):
+    """t.fill_(value), remembering the value on the host."""
+    t.fill_(value)
+    ver = _version(t)
+    if ver is None:
+        return
+    key = id(t)
+    _INDEX_MIRROR[key] = (weakref.ref(t, lambda _r, k=key: _INDEX_MIRROR.pop(k, None)), ver, int(value))
+
+
 def _fused_path(self, x):
     return x.dtype == torch.bfloat16 and all(
         t.dtype == torch.bfloat16 for t in (self.q.weight, self.k.weight, self.v.weight, self.norm_q.weight,
                                             self.norm_k.weight))
 
 
-def _se3_torch(x, prope_context, mode, frame_seqlen):
+def _se3_torch(x, prope_context, mode, frame_seqlen, t_bound=False):
     """The transform with torch ops, for modules outside the bf16 kernels' domain."""
     B, L, H, D = x.shape
     nf = L // frame_seqlen
     ctx = prope_context[:, -nf:].to(x.dtype)
+    if t_bound:
+        ctx = _bound_t(ctx)
     if mode == "P_inv":
         ctx = _invert_se3(ctx)
     xv = x.permute(0, 2, 1, 3).reshape(B, H, nf, frame_seqlen, D // 4, 4)
@@ -169,16 +228,19 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
     frame_seqlen = g0[1] * g0[2]
 
     delta = None
+    t_bound = _ref_flag(self, "_SE3_T_BOUND")
     if prope_context is not None:
         R_flat = prope_context[..., :3, :3].flatten(-2)
         t_vec = prope_context[..., :3, 3]
+        if _ref_flag(self, "_PROPE_LOG_T"):
+            t_vec = torch.sign(t_vec) * torch.log1p(t_vec.abs())
         c_all = torch.cat([R_flat, t_vec], dim=-1)
         T_half = s // frame_seqlen
         delta = self.pose_mlp(c_all[:, -T_half:])                  # [B, T, d/2] per-frame phase
         if fused:
-            v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen)
+            v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen, t_bound=t_bound)
         else:
-            v_p = _se3_torch(v, prope_context, "P_inv", frame_seqlen)
+            v_p = _se3_torch(v, prope_context, "P_inv", frame_seqlen, t_bound)
         v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
         if fused:
             v_rows = v.flatten(2)
@@ -192,11 +254,11 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
     g_start_f = current_start // frame_seqlen
     rsf = kv_cache.get("rope_start_frame") if isinstance(kv_cache, dict) else None
     if rsf is not None:
-        g_start_f = int(rsf.item())
+        g_start_f = read_index(rsf)
     grid = (max(1, num_new // frame_seqlen), g0[1], g0[2])
 
-    global_end = int(kv_cache["global_end_index"].item())
-    local_end_prev = int(kv_cache["local_end_index"].item())
+    global_end = read_index(kv_cache["global_end_index"])
+    local_end_prev = read_index(kv_cache["local_end_index"])
     if cache_local != -1 and cur_end > global_end and num_new + local_end_prev > kv_cache_size:
         n_evict = num_new + local_end_prev - kv_cache_size
         n_roll = local_end_prev - n_evict - sink_tokens
@@ -229,17 +291,17 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         yy = torch.empty((b, s, 2 * C), dtype=torch.bfloat16, device=x.device)
         y = yy[..., :C].view(b, s, n, d)
         chunk_attention(q, k_slice, v_slice, rope=rope, out=y)
-        se3_block_apply(y, prope_context, "P", frame_seqlen, out=yy[..., C:].view(b, s, n, d))
-        kv_cache["global_end_index"].fill_(cur_end)
-        kv_cache["local_end_index"].fill_(local_end)
+        se3_block_apply(y, prope_context, "P", frame_seqlen, out=yy[..., C:].view(b, s, n, d), t_bound=t_bound)
+        write_index(kv_cache["global_end_index"], cur_end)
+        write_index(kv_cache["local_end_index"], local_end)
         return torch.nn.functional.linear(yy, *_stacked_out(self))
     attn_out = chunk_attention(q, k_slice, v_slice, rope=rope).to(x.dtype)
-    kv_cache["global_end_index"].fill_(cur_end)
-    kv_cache["local_end_index"].fill_(local_end)
+    write_index(kv_cache["global_end_index"], cur_end)
+    write_index(kv_cache["local_end_index"], local_end)
 
     out = self.o(attn_out.flatten(2))
     if prope_context is not None:
-        x_p = _se3_torch(attn_out, prope_context, "P", frame_seqlen)
+        x_p = _se3_torch(attn_out, prope_context, "P", frame_seqlen, t_bound)
         out = out + self.prope_proj(x_p.flatten(2))
     return out
 

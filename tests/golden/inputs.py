@@ -156,3 +156,17 @@ def ulysses_shard(rank, world):
     B, L, H, D = ULYSSES_SHAPE
     g = torch.Generator().manual_seed(1000 + rank)
     return torch.randn(B, L // world, H, D, generator=g)
+
+
+# compressed pipeline (pipeline.npz): budget-split cases
+# (policy, budget_chunks, n_sink, recent_w, landmark_k, cache chunks or 0 = no cache given)
+BUDGET_CASES = [
+    ("v15b", 12, 1, 5, 30, 0), ("v15b", 24, 1, 7, 120, 0), ("v15b", 24, 1, 7, 10, 0), ("v15b", 3, 1, 5, 30, 0),
+    ("v15b", 2, 1, 5, 30, 0), ("v15b", 1, 1, 5, 30, 0), ("v15c", 12, 2, 5, 30, 0), ("consol", 12, 1, 5, 30, 0),
+    ("consol_div", 20, 4, 7, 30, 0), ("v15a", 20, 4, 7, 30, 0), ("v15b", 20, 1, 5, 30, 13),
+    ("v15b", 12, 1, 5, 30, 40), ("consol", 30, 1, 5, 8, 9), ("v15b", 9, 0, 4, 6, 0),
+]
+POLICIES = ["consol", "consol_div", "v15a", "v15b", "v15c"]
+# chunk-pose cases: (frames seen T, frames per chunk, prope_context dtype)
+POSE_CASES = [(3, 3, "float32"), (7, 3, "float32"), (12, 4, "float32"), (5, 1, "float32"), (9, 3, "bfloat16"),
+              (6, 3, "float64")]

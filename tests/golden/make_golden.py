@@ -25,6 +25,10 @@ tests); each fixture keeps a checksum of its inputs and the reference's outputs:
   ulysses.npz       wan_5b/distributed/util.all_to_all (seq->head and back)
                     over gloo process groups of 2 and 4 ranks (gloo lacks
                     all_to_all; it is emulated by its definition with all_gather)
+  pipeline.npz      the compressed pipeline's budget split (_init_compression_state)
+                    and chunk pose (_compute_chunk_pose), both compiled from the
+                    pipeline's source file and run on stub objects (importing the
+                    pipeline module would pull in the whole model stack)
 """
 import argparse
 import functools
@@ -272,14 +276,72 @@ def gen_ulysses(ref):
     np.savez_compressed(os.path.join(HERE, "ulysses.npz"), **out)
 
 
+def _compressed_methods(ref):
+    """_init_compression_state and _compute_chunk_pose of
+    CausalDiffusionInferenceCompressedPipeline, compiled from
+    pipeline/causal_diffusion_inference_compressed.py as plain functions."""
+    import ast
+    path = os.path.join(ref, "pipeline", "causal_diffusion_inference_compressed.py")
+    tree = ast.parse(open(path).read(), path)
+    cls = next(n for n in tree.body
+               if isinstance(n, ast.ClassDef) and n.name == "CausalDiffusionInferenceCompressedPipeline")
+    fns = [n for n in cls.body
+           if isinstance(n, ast.FunctionDef) and n.name in ("_init_compression_state", "_compute_chunk_pose")]
+    ns = {"np": np, "torch": torch}
+    exec(compile(ast.Module(body=fns, type_ignores=[]), path, "exec"), ns)
+    return ns["_init_compression_state"], ns["_compute_chunk_pose"]
+
+
+def gen_pipeline(ref):
+    import types as _t
+    import longctx.inference.landmark_cache as lc_mod
+    init_state, chunk_pose = _compressed_methods(ref)
+
+    made = []
+
+    class Recorder:
+        def __init__(self, **kw):
+            made.append(kw)
+
+    saved = lc_mod.LandmarkCache
+    lc_mod.LandmarkCache = Recorder
+    rows = []
+    try:
+        for policy, budget, n_sink, recent_w, landmark_k, cap_chunks in gi.BUDGET_CASES:
+            ct = 8
+            cfg = _t.SimpleNamespace(enabled=True, policy=policy, budget_chunks=budget, n_sink=n_sink,
+                                     recent_w=recent_w, landmark_k=landmark_k, landmark_eps=0.5, retrieve_k=6)
+            kv = [{"k": torch.empty(1, cap_chunks * ct, 1, 1)}] if cap_chunks else None
+            self_ = _t.SimpleNamespace(kvc_cfg=cfg, kv_cache_pos=kv, num_transformer_blocks=1)
+            made.clear()
+            init_state(self_, ct, 1, 1)
+            kw = made[0]
+            rows.append([gi.POLICIES.index(policy), budget, n_sink, recent_w, landmark_k, cap_chunks, ct,
+                         kw["n_sink"], kw["recent_w"], kw["K"], kw["retrieve_k"], 1 if kw["mode"] == "b" else 0,
+                         1 if kw["diverse"] else 0])
+    finally:
+        lc_mod.LandmarkCache = saved
+    out = {"budget": np.array(rows, dtype=np.int64)}
+    from reworld_b200.poses import random_walk
+    for i, (T, fpc, dt) in enumerate(gi.POSE_CASES):
+        ctx = torch.from_numpy(np.stack(random_walk(T, seed=40 + i, step_t=0.7, step_deg=12.0)))[None]
+        ctx = ctx.to(getattr(torch, dt))
+        out[f"pose{i}_ctx"] = ctx.float().numpy() if dt == "bfloat16" else ctx.numpy()
+        out[f"pose{i}_out"] = chunk_pose(None, ctx, fpc)
+    np.savez_compressed(os.path.join(HERE, "pipeline.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("REWORLD_REFERENCE"),
+                    required=not os.environ.get("REWORLD_REFERENCE"),
+                    help="path of the reference checkout (or set REWORLD_REFERENCE)")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     att = setup_reference(a.reference)
-    todo = a.only.split(",") if a.only else ["attention", "rope", "rmsnorm", "block", "self_attn", "landmark", "ulysses"]
+    todo = a.only.split(",") if a.only else ["attention", "rope", "rmsnorm", "block", "self_attn", "landmark", "ulysses",
+                                             "pipeline"]
     if "attention" in todo:
         gen_attention(att)
     if "rope" in todo:
@@ -294,6 +356,8 @@ def main():
         gen_landmark()
     if "ulysses" in todo:
         gen_ulysses(a.reference)
+    if "pipeline" in todo:
+        gen_pipeline(a.reference)
     print("golden fixtures written to", HERE)
 
 

@@ -6,7 +6,7 @@ memory behind its own allocator, or a real-time streaming loop where a cudaMallo
 rw_attn_fwd_noalloc keeps the key-split scratch in a fixed array inside the
 library.  These tests call it through the C ABI and check it against the
 regular entry point (caller-provided workspace) on two calls in a row, and that
-shapes needing more scratch than the array holds are refused.
+the array covers the scratch of every shape on this GPU.
 
 This file is named so that pytest collects it last.
 """
@@ -53,21 +53,25 @@ def test_noalloc_matches_regular_entry_point_on_two_calls(cuda, B, Lq, Lk, H):
     _native.check_status(cuda)
 
 
-def test_noalloc_refuses_shapes_beyond_its_scratch(cuda):
+def test_noalloc_scratch_array_covers_every_shape(cuda):
+    """The split needs 0 bytes or 2 slots of 133,120 bytes per resident pair,
+    whatever the shape (at most 74 pairs on a B200: 19.7 MB), so on this GPU no
+    shape reaches the RW_ERR_CAPACITY refusal; a sweep over batch, head and
+    length counts (the 704x1280 chunk and the B = 4, 66000-key stress shape
+    among them) checks that bound against the array's size."""
     from reworld_b200 import _native
     lib = _native.lib()
     cap = 80 * 1024 * 1024
-    shape = None
-    for H in range(1, 65):                         # find a head count whose split exceeds the array
-        if lib.rw_attn_workspace_bytes(1, 2048, 8192, H) > cap:
-            shape = (1, 2048, 8192, H)
-            break
-    if shape is None:
-        pytest.skip("no shape in the scan needs more scratch than the array on this GPU")
-    B, Lq, Lk, H = shape
-    q = torch.zeros(B, Lq, H, 128, dtype=torch.bfloat16, device=cuda)
-    k = torch.zeros(B, Lk, H, 128, dtype=torch.bfloat16, device=cuda)
-    out = torch.zeros_like(q)
-    st = _native.status_tensor(cuda)
-    assert _noalloc(lib, q, k, k, out, st, _native.stream_ptr(cuda)) == -5    # RW_ERR_CAPACITY
-    assert b"capacity" in lib.rw_error_string(-5)
+    slot_pair = 2 * (128 * 256 + 2 * 256) * 4          # two partial slots of one pair
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    seen = set()
+    for B in (1, 2, 4):
+        for H in (1, 3, 6, 12, 24, 40, 64):
+            for Lq, Lk in ((1, 1), (300, 1000), (660, 2640), (2640, 34320), (2640, 66000), (5280, 4096)):
+                need = lib.rw_attn_workspace_bytes(B, Lq, Lk, H)
+                assert need >= 0 and need % slot_pair == 0, (B, H, Lq, Lk, need)
+                assert need <= (sms // 2) * slot_pair <= cap, (B, H, Lq, Lk, need)
+                seen.add(need > 0)
+    assert seen == {False, True}                       # the sweep has shapes with and without a split
+    assert (sms // 2) * slot_pair < cap // 4           # a B200 uses under a quarter of the array
+    assert b"capacity" in lib.rw_error_string(-5)      # RW_ERR_CAPACITY, the refusal's message
