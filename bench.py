@@ -37,14 +37,22 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from reworld_b200.landmark import budget_split  # noqa: E402
+
 # workload: 704x1280 video, latent 44x80, 2x2 patches -> 22x40 tokens per frame, 3 frames per chunk
 FRAMES, TOK_H, TOK_W = 3, 22, 40
 CT = FRAMES * TOK_H * TOK_W                  # 2640 query tokens per chunk
 N_LAYERS, HEADS, HEAD_DIM = 30, 24, 128
-N_SINK, RECENT_W, N_LANDMARK, BANK_K = 1, 5, 6, 30
-BUDGET = N_SINK + RECENT_W + N_LANDMARK      # 12 chunks
+# the kv_compression knobs of the shipped v15b run (--kv_budget_chunks 12 --kv_n_sink 1 --kv_recent_w 5,
+# bank of 30); the pipeline's budget split turns them into sink 1 + recent 5 + 6 landmarks
+BUDGET_CHUNKS, SINK_KNOB, RECENT_CAP, LANDMARK_K, POLICY = 12, 1, 5, 30, "v15b"
+SPLIT = budget_split(BUDGET_CHUNKS, SINK_KNOB, RECENT_CAP, LANDMARK_K, POLICY,
+                     cache_tokens=(BUDGET_CHUNKS + 1) * CT, chunk_tokens=CT)
+N_SINK, RECENT_W, N_LANDMARK, BANK_K = SPLIT.n_sink, SPLIT.recent_w, SPLIT.n_landmark, SPLIT.K
+BUDGET = SPLIT.budget                        # 12 chunks
 LK = (BUDGET + 1) * CT                       # 34320 keys (cache + the chunk itself)
 FORWARDS_PER_CHUNK = 5                       # 4 denoise + 1 clean-KV forward
+REVISIT_EVERY = 8                            # chunks between returns to an earlier place
 METRIC = "causal chunk-attn TFLOP/s + ms/chunk, 704x1280 12-chunk KV, 1/2/4/8 B200"
 WORKLOAD = ("704x1280 chunk (3 latent frames, 2640 tokens) x 30 layers x 24 heads x 128, KV budget 12 chunks "
             "(1 sink + 5 recent + 6 landmarks = 31680 keys) + the chunk itself = 34320 keys; 5 forwards/chunk "
@@ -146,7 +154,6 @@ class Rollout:
 
     def __init__(self, device, heads, seq_shard, world, rank, group):
         from reworld_b200 import RopeArgs, build_freqs, device_table
-        from reworld_b200.landmark import LandmarkBankStack
         from reworld_b200.poses import random_walk
         self.dev, self.H, self.world, self.rank, self.group = device, heads, world, rank, group
         self.cap = (BUDGET + 1) * CT
@@ -168,16 +175,30 @@ class Rollout:
         self.k = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
         self.v = [torch.randn(shape, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
         self.out = [torch.empty(1, CT, heads, HEAD_DIM, dtype=torch.bfloat16, device=device) for _ in range(N_LAYERS)]
-        self.bank = LandmarkBankStack(CT, N_LAYERS, heads, HEAD_DIM, n_sink=N_SINK, recent_w=RECENT_W, K=BANK_K,
-                                      retrieve_k=N_LANDMARK, mode="b", device=device)
+        self.bank = None
+        self.new_bank()
         self.table = device_table(build_freqs(HEAD_DIM, 12 / 22, 20 / 40), device)
         self.RopeArgs = RopeArgs
-        self.poses = random_walk(4096, seed=0, revisit_every=8)
-        self.chunk = 0
-        self.tot = 0
+        # camera context of every frame (the model's prope_context), on the device as in the
+        # pipeline; the bank's pose of a chunk is chunk_pose over its frames
+        frames = random_walk(512 * FRAMES, seed=0, step_t=0.1 / FRAMES, step_deg=5.0 / FRAMES,
+                             revisit_every=REVISIT_EVERY * FRAMES)
+        self.frame_ctx = torch.from_numpy(np.stack(frames)).to(device).unsqueeze(0)
         self.launches = 0
+        self.flops_all = 0.0          # attention FLOPs of all heads issued so far (whole job)
         self._split_cache = {}
         self.attn_events = []
+
+    def new_bank(self):
+        """A cold bank (budget split of the v15b knobs) and an empty cache."""
+        from reworld_b200.landmark import LandmarkBankStack
+        self.bank = None
+        torch.cuda.empty_cache()
+        self.bank = LandmarkBankStack.from_budget(CT, N_LAYERS, self.H, HEAD_DIM, BUDGET_CHUNKS, SINK_KNOB,
+                                                  RECENT_CAP, LANDMARK_K, POLICY, cache_tokens=self.cap,
+                                                  device=self.dev)
+        self.chunk = 0
+        self.tot = 0
 
     def fill_bank(self, n_chunks):
         """Cold-start the cache: run the bank update for n_chunks (no attention)."""
@@ -188,8 +209,9 @@ class Rollout:
             self.bank_update()
 
     def bank_update(self):
+        from reworld_b200.landmark import chunk_pose
         c = self.chunk
-        pose = self.poses[c]
+        pose = chunk_pose(self.frame_ctx[:, :(c + 1) * FRAMES], FRAMES)
         src_k = [ck[0, self.tot:self.tot + CT] for ck in self.cache_k]
         src_v = [cv[0, self.tot:self.tot + CT] for cv in self.cache_v]
         R = self.bank.add_chunk_from(src_k, src_v, pose, pose)
@@ -204,6 +226,7 @@ class Rollout:
         for l in range(N_LAYERS):
             q, k, v = self.q[l], self.k[l], self.v[l]
             lk = self.tot + CT
+            self.flops_all += attn_flops(CT, lk, HEADS)
             if self.sp is not None:
                 # peer-memory exchange: scatter q/k/v (RoPE + cache write fused), barrier,
                 # attention on the local heads, scatter the output back, barrier
@@ -285,7 +308,8 @@ def run_gpu(args):
     ms_max = float(t.item())
 
     # e2e: host buffers through the public API, copies inside the timed region
-    e2e = run_e2e(ro, args, dev) if world == 1 else None
+    e2e = run_e2e(ro, args, dev) if world == 1 else run_e2e_sp(ro, args, dev)
+    parity = sp_parity(ro, dev, world, rank, group) if world > 1 else None
 
     step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
@@ -296,6 +320,7 @@ def run_gpu(args):
     extra = {}
     if rank == 0 and world == 1:
         extra = gpu_side_baselines(ro, dev)
+    cold = rollout_cold(ro, dev, world, group, n_chunks=32)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(step_flops / (ms_max * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -319,6 +344,9 @@ def run_gpu(args):
         }
         if e2e is not None:
             line["e2e"] = e2e
+        if parity is not None:
+            line["sp_parity"] = parity
+        line["rollout_cold32"] = cold
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
@@ -398,6 +426,157 @@ def run_e2e(ro, args, dev):
                     "copies on side streams overlapped with compute"}
 
 
+def rollout_cold(ro, dev, world, group, n_chunks=32):
+    """The streaming rollout from a cold cache: a new bank, then n_chunks chunks
+    (5 forwards x 30 layers each, attention over the cache as it fills, bank
+    update, a return to an earlier place every 8 chunks), timed as one region
+    with CUDA events (max over ranks)."""
+    import torch.distributed as dist
+    ro.new_bank()
+    f0 = ro.flops_all
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n_chunks):
+        ro.step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    ms = float(t.item())
+    fl = ro.flops_all - f0
+    return {"chunks": n_chunks, "ms": round(ms, 2), "chunks_per_s": round(n_chunks / (ms * 1e-3), 3),
+            "ms_per_chunk": round(ms / n_chunks, 3), "attn_tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+            "n_gpus": world, "final_keys": ro.tot + CT,
+            "workload": (f"cold start: {n_chunks} chunks of 704x1280 ({CT} tokens), {FORWARDS_PER_CHUNK} forwards x "
+                         f"{N_LAYERS} layers each, KV budget {BUDGET} = {N_SINK} sink + {RECENT_W} recent + "
+                         f"{N_LANDMARK} landmarks from a {BANK_K}-entry bank, camera returns every "
+                         f"{REVISIT_EVERY} chunks; keys grow from {CT} to {LK}")}
+
+
+def sp_parity(ro, dev, world, rank, group):
+    """One layer through the Ulysses path (seq->head scatter with the RoPE and cache
+    write, attention on this rank's heads, output rows to their owners) against
+    this package's single-GPU attention over all 24 heads on the same inputs:
+    every rank rebuilds the whole layer (all tokens' q/k/v, every rank's cached
+    rows) and compares its token shard.  Outside the timed region."""
+    import torch.distributed as dist
+    from reworld_b200 import chunk_attention, rope_kv_store
+    l = 0
+    Ls, Hp = CT // world, HEADS // world
+    start_frame = (ro.chunk * CT) // (TOK_H * TOK_W)
+    rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
+    tot = ro.tot
+
+    def gather_seq(x):                 # [1, Ls, H, D] per rank -> [1, CT, H, D]
+        buf = torch.empty((world * Ls, HEADS, HEAD_DIM), dtype=x.dtype, device=dev)
+        dist.all_gather_into_tensor(buf, x[0].contiguous(), group=group)
+        return buf.unsqueeze(0)
+
+    def gather_heads(x):               # [1, n, Hp, D] per rank -> [1, n, H, D]
+        n = x.shape[1]
+        buf = torch.empty((world, n, Hp, HEAD_DIM), dtype=x.dtype, device=dev)
+        dist.all_gather_into_tensor(buf, x[0].contiguous(), group=group)
+        return buf.permute(1, 0, 2, 3).reshape(1, n, HEADS, HEAD_DIM)
+
+    q_full, k_full, v_full = gather_seq(ro.q[l]), gather_seq(ro.k[l]), gather_seq(ro.v[l])
+    ck = torch.zeros((1, tot + CT, HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    cv = torch.zeros_like(ck)
+    ck[:, :tot] = gather_heads(ro.cache_k[l][:, :tot])
+    cv[:, :tot] = gather_heads(ro.cache_v[l][:, :tot])
+    rope_kv_store(k_full, v_full, ck, cv, tot, rope=rope)
+    ref = chunk_attention(q_full, ck, cv, rope=rope)[:, rank * Ls:(rank + 1) * Ls].float()
+    y = ro.sp.layer(l, ro.q[l], ro.k[l], ro.v[l], tot, rope=rope).float()
+    torch.cuda.synchronize()
+    kdiff = (ro.cache_k[l][:, tot:tot + CT].float() - ck[:, tot:tot + CT, rank * Hp:(rank + 1) * Hp].float()).abs()
+    err = (y - ref).abs()
+    st = torch.tensor([err.max().item(), err.mean().item(), kdiff.max().item()], device=dev)
+    mx = st.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(st, op=dist.ReduceOp.SUM, group=group)
+    ok = mx[0].item() < 2e-2 and st[1].item() / world < 2e-3 and mx[2].item() == 0.0
+    return {"layer": l, "keys": tot + CT, "max_abs": round(mx[0].item(), 6), "mean_abs": round(st[1].item() / world, 7),
+            "cache_rows_max_abs": mx[2].item(), "tolerance": "max-abs 2e-2, mean-abs 2e-3; cache rows exact",
+            "pass": bool(ok),
+            "against": "reworld_b200.chunk_attention over all 24 heads on one GPU (q/k/v and cached rows of "
+                       "every rank gathered), k rows roped by rw_rope_kv_store"}
+
+
+def run_e2e_sp(ro, args, dev):
+    """The Ulysses chunk step end to end: every rank's q/k/v sequence shard of every
+    layer and forward arrives from pinned host memory, and its output shard goes
+    back to pinned host memory (copies on side streams; the output is first moved
+    off the shared exchange buffer on the compute stream)."""
+    import torch.distributed as dist
+    world = ro.world
+    Ls = CT // world
+    comp = torch.cuda.current_stream(dev)
+    h2d = torch.cuda.Stream(dev)
+    d2h = torch.cuda.Stream(dev)
+    shape = (1, Ls, HEADS, HEAD_DIM)
+    host_in = [torch.randn(3, *shape).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    host_out = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dev_in = [torch.empty((3, *shape), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dev_out = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_read = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_used + ev_read:
+        e.record(comp)
+    bytes_in = 3 * Ls * HEADS * HEAD_DIM * 2
+    bytes_out = Ls * HEADS * HEAD_DIM * 2
+
+    def step():
+        n = 0
+        for _f in range(FORWARDS_PER_CHUNK):
+            start_frame = (ro.chunk * CT) // (TOK_H * TOK_W)
+            rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
+            for l in range(N_LAYERS):
+                b = n & 1
+                with torch.cuda.stream(h2d):
+                    h2d.wait_event(ev_used[b])
+                    dev_in[b].copy_(host_in[b], non_blocking=True)
+                    ev_in[b].record(h2d)
+                comp.wait_event(ev_in[b])
+                comp.wait_event(ev_read[b])
+                y = ro.sp.layer(l, dev_in[b][0], dev_in[b][1], dev_in[b][2], ro.tot, rope=rope)
+                dev_out[b].copy_(y)
+                ev_used[b].record(comp)
+                ev_out[b].record(comp)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_out[b])
+                    host_out[b].copy_(dev_out[b], non_blocking=True)
+                    ev_read[b].record(d2h)
+                n += 1
+        ro.bank_update()
+
+    for _ in range(max(1, args.warmup // 2)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(comp)
+    for _ in range(args.steps):
+        step()
+    comp.wait_stream(d2h)
+    t1.record(comp)
+    torch.cuda.synchronize()
+    t = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
+    n_io = FORWARDS_PER_CHUNK * N_LAYERS
+    return {"value": round(step_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 3),
+            "h2d_bytes_per_step": n_io * bytes_in * world, "d2h_bytes_per_step": n_io * bytes_out * world,
+            "path": "UlyssesP2P.layer with every rank's pinned host q/k/v shard in and output shard out, copies "
+                    "on side streams; bytes summed over ranks"}
+
+
 def gpu_side_baselines(ro, dev):
     """Library attention on the same single-layer shape, for context: flash-attn 2
     (what the reference's attention() dispatches to on a GPU with the wheel
@@ -410,6 +589,7 @@ def gpu_side_baselines(ro, dev):
     k = ro.cache_k[l][:, :LK].contiguous()
     v = ro.cache_v[l][:, :LK].contiguous()
     fl = attn_flops(CT, LK, HEADS)
+    out["attn_ab"] = attention_ab(ro, dev)
 
     def timeit(fn, n=10):
         for _ in range(3):
@@ -459,6 +639,54 @@ def gpu_side_baselines(ro, dev):
     out["text_cross_attn_tflops"] = round(attn_flops(CT, 512, HEADS) / msx / 1e9, 1)
     out["block_ffn"] = ffn_measure(dev, timeit)
     return out
+
+
+def attention_ab(ro, dev, reps=7, calls=6, n_inputs=3):
+    """This package's chunk attention against the library attention the reference
+    would run on this GPU (torch SDPA: cuDNN here; flash-attn 2, the wheel the
+    reference's attention() dispatches to), A/B interleaved: `reps` rounds, each
+    timing `calls` back-to-back calls of every arm in turn on the same inputs,
+    which rotate over n_inputs layers' q and contiguous K/V (422 MB each, so
+    every call reads from HBM).  Reports each arm's median round."""
+    from reworld_b200 import chunk_attention
+    fl = attn_flops(CT, LK, HEADS)
+    sets = []
+    for i in range(n_inputs):
+        l = i % N_LAYERS
+        sets.append((ro.q[l], ro.cache_k[l][:, :LK].contiguous(), ro.cache_v[l][:, :LK].contiguous()))
+    sdpa_sets = [(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)) for q, k, v in sets]
+    outs = [torch.empty_like(q) for q, _, _ in sets]
+    arms = {"reworld_b200": lambda i: chunk_attention(*sets[i], out=outs[i]),
+            "torch_sdpa": lambda i: torch.nn.functional.scaled_dot_product_attention(*sdpa_sets[i])}
+    try:
+        import flash_attn
+        arms["flash_attn2"] = lambda i: flash_attn.flash_attn_func(*sets[i])
+    except Exception:   # noqa: BLE001 - the wheel is optional
+        pass
+    for fn in arms.values():                      # warm-up (library autotuning, workspace growth)
+        for i in range(n_inputs):
+            fn(i)
+    torch.cuda.synchronize()
+    times = {name: [] for name in arms}
+    for _ in range(reps):
+        for name, fn in arms.items():
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for c in range(calls):
+                fn(c % n_inputs)
+            b.record()
+            b.synchronize()
+            times[name].append(a.elapsed_time(b) / calls)
+    res = {}
+    for name, ts in times.items():
+        med = statistics.median(ts)
+        res[name] = {"median_ms": round(med, 4), "tflops": round(fl / med / 1e9, 1),
+                     "rounds_ms": [round(t, 4) for t in ts]}
+    res["speedup_vs_torch_sdpa"] = round(res["torch_sdpa"]["median_ms"] / res["reworld_b200"]["median_ms"], 3)
+    res["shape"] = f"q [1, {CT}, {HEADS}, {HEAD_DIM}], k/v [1, {LK}, {HEADS}, {HEAD_DIM}] bf16"
+    res["method"] = (f"{reps} interleaved rounds of {calls} calls per arm, inputs rotating over {n_inputs} "
+                     f"layers (each > L2); median round")
+    return res
 
 
 def ffn_measure(dev, timeit, ffn_dim=14336):
