@@ -638,7 +638,140 @@ def gpu_side_baselines(ro, dev):
     out["text_cross_attn_ms"] = round(msx, 4)
     out["text_cross_attn_tflops"] = round(attn_flops(CT, 512, HEADS) / msx / 1e9, 1)
     out["block_ffn"] = ffn_measure(dev, timeit)
+    out["gemm"] = gemm_ab(dev)
+    out["dropin_layer"] = dropin_layer_measure(ro, dev)
     return out
+
+
+def gemm_ab(dev, reps=9, calls=8, n_inputs=3):
+    """rw_gemm_bf16 against cuBLAS (torch.nn.functional.linear) on the projections of
+    one layer-chunk (2640 tokens, width 3072): the stacked q|k|v GEMM, value_proj,
+    the stacked o|prope_proj GEMM over [y | P y], and the FFN pair (the first with the
+    tanh GELU: in the epilogue here, a separate torch op after cuBLAS).  Interleaved
+    rounds on inputs rotating over n_inputs copies; median round per arm."""
+    from reworld_b200.gemm import linear
+    C = HEADS * HEAD_DIM
+    shapes = [("qkv", CT, 3 * C, C, False), ("value_proj", CT, C, C, False), ("o_prope", CT, C, 2 * C, False),
+              ("ffn_up_gelu", CT, 14336, C, True), ("ffn_down", CT, C, 14336, False)]
+    burst = load_peaks()[0]
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(9)
+    for name, M, N, K, gelu in shapes:
+        xs = [torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(n_inputs)]
+        ws = [(torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_inputs)]
+        bs = [(torch.randn(N, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_inputs)]
+        outs = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for _ in range(n_inputs)]
+
+        def ours(i, gelu=gelu):
+            linear(xs[i], ws[i], bs[i], gelu=gelu, out=outs[i])
+
+        def cublas(i, gelu=gelu):
+            y = torch.nn.functional.linear(xs[i], ws[i], bs[i])
+            if gelu:
+                torch.nn.functional.gelu(y, approximate="tanh")
+
+        arms = {"reworld_b200": ours, "cublas": cublas}
+        for f in arms.values():
+            for i in range(n_inputs):
+                f(i)
+        torch.cuda.synchronize()
+        times = {a: [] for a in arms}
+        for _ in range(reps):
+            for a, f in arms.items():
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for c in range(calls):
+                    f(c % n_inputs)
+                e1.record()
+                e1.synchronize()
+                times[a].append(e0.elapsed_time(e1) / calls)
+        fl = 2.0 * M * N * K
+        r = {"shape": f"[{M}, {K}] x [{N}, {K}]^T" + (" + GELU(tanh)" if gelu else "")}
+        for a, ts in times.items():
+            med = statistics.median(ts)
+            r[a] = {"us": round(med * 1e3, 1), "tflops": round(fl / med / 1e9, 1)}
+        r["ratio_vs_cublas"] = round(statistics.median(times["cublas"]) / statistics.median(times["reworld_b200"]), 3)
+        r["frac_of_bf16_burst"] = round(fl / statistics.median(times["reworld_b200"]) / 1e9 / burst, 4)
+        res[name] = r
+    res["method"] = f"{reps} interleaved rounds of {calls} calls per arm, median; inputs rotate over {n_inputs} copies"
+    return res
+
+
+def dropin_layer_measure(ro, dev, n_calls=6):
+    """One layer of the installed self-attention drop-in (prop_self_attn_forward at
+    the 5B width: 3072 channels, 24 heads, a 2640-token chunk over a 12-chunk cache,
+    with a camera context so the PRoPE path runs) called the way the reference model
+    calls it, with its input x copied from pinned host memory and its output copied
+    back to pinned host memory inside the timed region: the plugin's own overheads
+    (index bookkeeping, launches, host work) included.  Per call, against the
+    attention kernel alone on the same shape."""
+    import torch.nn as nn
+    from reworld_b200.self_attn import install
+    from reworld_b200.poses import random_walk
+    C = HEADS * HEAD_DIM
+
+    class _RMS(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.eps = 1e-6
+            self.weight = nn.Parameter(torch.ones(C))
+
+    class _Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.num_heads, self.head_dim = HEADS, HEAD_DIM
+            self.local_attn_size, self.sink_size, self.max_attention_size = -1, 0, None
+            self.q, self.k, self.v, self.o = (nn.Linear(C, C) for _ in range(4))
+            self.norm_q, self.norm_k = _RMS(), _RMS()
+            self.pose_mlp = nn.Sequential(nn.Linear(12, 256), nn.SiLU(), nn.Linear(256, HEAD_DIM // 2))
+            self.value_proj, self.prope_proj = nn.Linear(C, C), nn.Linear(C, C)
+
+    g = torch.Generator().manual_seed(4)
+    mod = _Attn()
+    with torch.no_grad():
+        for p_ in mod.parameters():
+            p_.copy_(torch.randn(p_.shape, generator=g) * 0.02)
+    mod = mod.to(device=dev, dtype=torch.bfloat16)
+    install([type("Blk", (), {"self_attn": mod})()])
+    n0 = LK - CT
+    cache = {"k": ro.cache_k[0], "v": ro.cache_v[0], "global_end_index": torch.tensor([n0], device=dev),
+             "local_end_index": torch.tensor([n0], device=dev)}
+    frames = random_walk(n0 // (TOK_H * TOK_W) + FRAMES, seed=3)
+    ctx = torch.from_numpy(np.stack(frames)).unsqueeze(0).to(device=dev, dtype=torch.bfloat16)
+    freqs = __import__("reworld_b200").build_freqs(HEAD_DIM, 12 / 22, 20 / 40)
+    x_host = torch.randn(1, CT, C).to(torch.bfloat16).pin_memory()
+    y_host = torch.empty(1, CT, C, dtype=torch.bfloat16).pin_memory()
+    seq_lens, grid = torch.tensor([CT]), torch.tensor([[FRAMES, TOK_H, TOK_W]])
+
+    def call():
+        cache["global_end_index"].fill_(n0)      # the same chunk position every call
+        cache["local_end_index"].fill_(n0)
+        x = x_host.to(dev, non_blocking=True)
+        y = mod.forward(x, seq_lens, grid, freqs, None, kv_cache=cache, current_start=n0, prope_context=ctx)
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(2):
+            call()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n_calls):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / n_calls
+    ms = e0.elapsed_time(e1) / n_calls
+    fl_attn = attn_flops(CT, LK, HEADS)
+    fl_proj = 2.0 * CT * C * (3 * C + C + 2 * C)           # q|k|v, value_proj, o|prope_proj
+    return {"ms_per_layer": round(ms, 4), "host_wall_ms_per_layer": round(wall * 1e3, 4),
+            "tflops": round((fl_attn + fl_proj) / (ms * 1e-3) / 1e12, 1),
+            "h2d_bytes": CT * C * 2, "d2h_bytes": CT * C * 2,
+            "path": "installed prop_self_attn_forward (stacked q|k|v GEMM, fused RMSNorm/RoPE/cache store, PRoPE "
+                    "SE3 + value_proj GEMM with residual, attention, [y | P y] GEMM) with x from pinned host memory "
+                    "and the output to pinned host memory",
+            "shape": f"x [1, {CT}, {C}], cache {LK} keys x {HEADS} heads, PRoPE context on"}
 
 
 def attention_ab(ro, dev, reps=7, calls=6, n_inputs=3):
@@ -691,8 +824,9 @@ def attention_ab(ro, dev, reps=7, calls=6, n_inputs=3):
 
 def ffn_measure(dev, timeit, ffn_dim=14336):
     """The DiT block's norm2 + FFN on one layer's chunk [2640, 3072]: the LayerNorm row
-    kernel, and GeluFFN (GELU in the first GEMM's cuBLASLt epilogue) against the
-    reference's Linear -> GELU(tanh) -> Linear, both on the same bf16 weights."""
+    kernel, and GeluFFN (two rw_gemm_bf16 GEMMs, the GELU in the first one's
+    epilogue) against the reference's Linear -> GELU(tanh) -> Linear (cuBLAS and a
+    torch GELU), both on the same bf16 weights."""
     import torch.nn as nn
     from reworld_b200.block import GeluFFN, row_norm
     C = HEADS * HEAD_DIM
@@ -717,10 +851,10 @@ def ffn_measure(dev, timeit, ffn_dim=14336):
     burst, sustained, hbm, peak_src = load_peaks()
     nb = 2 * CT * C * 2
     return {"ffn_ms": round(ms_f, 4), "ffn_tflops": round(fl / ms_f / 1e9, 1),
-            "frac_of_bf16_burst": round(fl / ms_f / 1e9 / burst, 4), "unfused_ffn_ms": round(ms_u, 4),
+            "frac_of_bf16_burst": round(fl / ms_f / 1e9 / burst, 4), "reference_ffn_ms": round(ms_u, 4),
             "layer_norm_ms": round(ms_n, 4), "layer_norm_gbs": round(nb / (ms_n * 1e-3) / 1e9, 1),
             "shape": f"[{CT}, {C}] -> {ffn_dim} -> {C}, bf16; inputs rotate over 8 chunks",
-            "peak_kind": f"cuBLAS bf16 burst ({peak_src})"}
+            "peak_kind": f"cuBLAS bf16 burst ({peak_src})", "reference_ffn": "nn.Sequential on cuBLAS + torch GELU"}
 
 
 def host_tier_measure(dev, n_layers=2, chunks=20):

@@ -296,6 +296,32 @@ int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, 
                    const unsigned long long* out_ptrs, int P, int rank, int H, float softmax_scale,
                    const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status, void* stream);
 
+/* Dense bf16 GEMM on CTA pairs (2-SM tcgen05.mma, TMA-fed stages, fp32
+ * accumulation in tensor memory):
+ *   C[M, N] = A[M, K] B[N, K]^T                       RW_GEMM_EPI_NONE
+ *           = A B^T + bias[N]                          RW_GEMM_EPI_BIAS
+ *           = gelu_tanh(A B^T + bias)                  RW_GEMM_EPI_BIAS_GELU
+ *           = R[M, N] + bf16(A B^T + bias)             RW_GEMM_EPI_BIAS_RESIDUAL
+ * i.e. torch.nn.functional.linear(A, B, bias) with B an nn.Linear weight [out,
+ * in] (one rounding to bf16; the residual form rounds twice, as torch's bf16
+ * `r + linear(x)`; R may alias C).  Replaces the reference's nn.Linear calls
+ * around the chunk attention: the q/k/v projections
+ * (wan_5b/modules/action_model.py:164-166, as one GEMM over the stacked [3C, C]
+ * weight), value_proj with its residual (:203), o + prope_proj (:308-318, one
+ * GEMM over [y | P y] and the stacked [C, 2C] weight) and the block's FFN
+ * Linear -> GELU(tanh) -> Linear (:547-556).
+ * Requirements: bf16 row-major operands with 16-byte aligned bases, row strides
+ * (elements) multiples of 8 with lda, ldb >= K, ldc, ldr >= N; K a multiple of
+ * 64 and N of 128 (RW_ERR_UNSUPPORTED otherwise); bias (when used) 16-byte
+ * aligned. */
+#define RW_GEMM_EPI_NONE 0
+#define RW_GEMM_EPI_BIAS 1
+#define RW_GEMM_EPI_BIAS_GELU 2
+#define RW_GEMM_EPI_BIAS_RESIDUAL 3
+int rw_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, const void* bias, const void* R,
+                 long long ldr, void* C, long long ldc, int M, int N, int K, int epilogue, int* status,
+                 void* stream);
+
 /* Human-readable text of an RW_ERR_* code. */
 const char* rw_error_string(int code);
 

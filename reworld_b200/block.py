@@ -11,12 +11,13 @@ with norm3 / norm2 WanLayerNorm (model.py:92-102), cross_attn a
 MultiShotT2VCrossAttention (causal_model.py:186-289; WanCrossAttention,
 model.py:162-197) and ffn Linear(dim, ffn_dim) -> GELU(tanh) -> Linear(ffn_dim, dim)
 (action_model.py:404-406).  `install(model)` swaps, per block, norm2 / norm3 for
-`RowLayerNorm` (rw_row_norm), ffn for `GeluFFN` (the first GEMM with the GELU in
-cuBLASLt's epilogue, then the second GEMM) and cross_attn.forward for
-`cross_attn_forward` (norm_q / norm_k on rw_row_norm, the attention on the
-package's kernel with k_lens).  The modulation and the residual adds stay the
-reference's own elementwise ops.  CUDA tensors only; bf16 modules run the
-kernels, modules in other dtypes keep their own computation.
+`RowLayerNorm` (rw_row_norm), ffn for `GeluFFN` (the package's tcgen05 GEMM,
+rw_gemm_bf16, with the GELU in the first GEMM's epilogue, then the second GEMM)
+and cross_attn.forward for `cross_attn_forward` (its q/k/v/o projections on the
+same GEMM, norm_q / norm_k on rw_row_norm, the attention on the package's kernel
+with k_lens).  The modulation and the residual adds stay the reference's own
+elementwise ops.  CUDA tensors only; bf16 modules run the kernels, modules in
+other dtypes keep their own computation.
 """
 import types
 
@@ -24,6 +25,7 @@ import torch
 import torch.nn as nn
 
 from . import _native
+from . import gemm
 from ._native import c_vp
 from .attention import attention
 
@@ -75,8 +77,8 @@ class RowLayerNorm(nn.Module):
 
 
 class GeluFFN(nn.Module):
-    """Linear -> GELU(tanh) -> Linear with the GELU applied in the first GEMM's
-    epilogue (cuBLASLt, on the fp32 accumulator: one rounding instead of the
+    """Linear -> GELU(tanh) -> Linear on rw_gemm_bf16, the GELU applied in the first
+    GEMM's epilogue (on the fp32 accumulator: one rounding instead of the
     reference's two); keeps the wrapped Sequential's parameters."""
 
     def __init__(self, seq):
@@ -90,9 +92,8 @@ class GeluFFN(nn.Module):
         if x.dtype != torch.bfloat16 or getattr(act, "approximate", "none") != "tanh" or \
                 not _bf16_or_none(lin1.weight, lin1.bias, lin2.weight, lin2.bias):
             return self.inner(x)
-        x2 = x.reshape(-1, x.shape[-1])
-        h = torch._addmm_activation(lin1.bias, x2, lin1.weight.t(), use_gelu=True)
-        return nn.functional.linear(h, lin2.weight, lin2.bias).view(*x.shape[:-1], -1)
+        h = gemm.module_linear(lin1, x, gelu=True)
+        return gemm.module_linear(lin2, h)
 
 
 def cross_attn_forward(self, x, context, context_lens, is_teacher_forcing=False, crossattn_cache=None):
@@ -116,19 +117,23 @@ def cross_attn_forward(self, x, context, context_lens, is_teacher_forcing=False,
             return row_norm(t, mod.weight, None, mod.eps, "rms")
         return mod(t)
 
+    def lin(mod, t):
+        # bf16 projections on the package's GEMM; other dtypes keep the module's own
+        return gemm.module_linear(mod, t) if fused and t.dtype == torch.bfloat16 else mod(t)
+
     def cross_attend(xc):
         b_eff = xc.size(0)
-        q = norm(self.q(xc), self.norm_q).view(b_eff, -1, n, d)
+        q = norm(lin(self.q, xc), self.norm_q).view(b_eff, -1, n, d)
         if crossattn_cache is not None and crossattn_cache["is_init"]:
             k, v = crossattn_cache["k"], crossattn_cache["v"]
         else:
-            k = norm(self.k(context), self.norm_k).view(b_eff, -1, n, d)
-            v = self.v(context).view(b_eff, -1, n, d)
+            k = norm(lin(self.k, context), self.norm_k).view(b_eff, -1, n, d)
+            v = lin(self.v, context).view(b_eff, -1, n, d)
             if crossattn_cache is not None:
                 crossattn_cache["is_init"] = True
                 crossattn_cache["k"], crossattn_cache["v"] = k, v
         o = attention(q, k, v, k_lens=context_lens)
-        return self.o(o.flatten(2))
+        return lin(self.o, o.flatten(2))
 
     def chunk_and_attend(xp):
         Lp = xp.size(1)

@@ -367,6 +367,18 @@ __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// 2-D tiled load into this CTA's shared memory, completion (bytes) counted on the
+// mbarrier at shared::cluster address `bar_cluster` (the even CTA's for a pair).
+// No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (tcgen05 format, version 1).
 // layout 2 = 128-byte swizzle.  lbo/sbo in bytes.

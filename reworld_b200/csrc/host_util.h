@@ -54,6 +54,23 @@ inline int make_bf16_bl_hd_map(CUtensorMap* m, const void* ptr, int B, int L, in
   return r == CUDA_SUCCESS ? 0 : -4;
 }
 
+// Row-major bf16 matrix [rows, cols] (row stride ld elements) described to TMA as
+// dims (cols, rows), tiled in boxes of 64 columns x box_rows rows with 128-byte
+// swizzle (one box row = 128 bytes); rows past the end read as zero.
+inline int make_bf16_2d_map(CUtensorMap* m, const void* ptr, long long rows, long long cols, long long ld,
+                            int box_rows) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return -4;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -4;
+}
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 // Host threads may race here: the attribute call is idempotent and the mask is
 // atomic, so a second thread at worst repeats the call.

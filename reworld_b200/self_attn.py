@@ -9,12 +9,14 @@ P^-1 residual when prope_context is given, the chunk's RoPE at its start frame
 [local_end - num_new, local_end), attention over kv_cache[:, :local_end], the
 index updates of :304-305 and the o projection (+ P residual).
 
-What runs on the B200 kernels: for a bf16 module, the RMSNorm of q and k, the
-RoPE of k and the cache write of k/v (one rw_qkv_norm_rope_store launch; a
-module in another dtype keeps torch's norm and uses rw_rope_kv_store), and the
-attention with q's RoPE applied inside the kernel (rw_attn_fwd).  The q/k/v
-projections run as one cuBLAS GEMM over the stacked weights; the PRoPE residual
-matmuls stay torch GPU ops.  The KV cache must be bf16.
+What runs on the B200 kernels for a bf16 module: the q/k/v projections as one
+rw_gemm_bf16 GEMM over the stacked weights, the RMSNorm of q and k, the RoPE of k
+and the cache write of k/v (one rw_qkv_norm_rope_store launch), the PRoPE SE3
+transforms (rw_se3_block_apply) with value_proj and its residual as one GEMM
+written in place, the attention with q's RoPE applied inside the kernel
+(rw_attn_fwd), and o(y) + prope_proj(P y) as one GEMM over [y | P y].  A module
+in another dtype keeps torch's projections and norm, casts q/k/v to bf16 and uses
+rw_rope_kv_store and the attention kernel.  The KV cache must be bf16.
 
 Install it per block the way the reference installs its sequence-parallel
 forward (wan_5b/text2video.py:150-154): `install(model)`.
@@ -27,6 +29,7 @@ import weakref
 import torch
 
 from . import _native
+from . import gemm
 from ._native import c_vp
 from .attention import chunk_attention
 from .kv_cache import qkv_norm_rope_store, rope_kv_store
@@ -217,7 +220,7 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
     fused = _fused_path(self, x)
     if fused:
         C = n * d
-        qkv = torch.nn.functional.linear(x, *_stacked_qkv(self))        # [b, s, 3C]
+        qkv = gemm.linear(x, *_stacked_qkv(self))                       # [b, s, 3C]
         q_rows, k_rows, v_rows = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
         v = v_rows.view(b, s, n, d)
     else:
@@ -238,12 +241,13 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         T_half = s // frame_seqlen
         delta = self.pose_mlp(c_all[:, -T_half:])                  # [B, T, d/2] per-frame phase
         if fused:
+            # v + value_proj(P^-1 v): one GEMM whose epilogue adds the residual (two
+            # roundings, as the reference's bf16 add) in place into the v columns
             v_p = se3_block_apply(v, prope_context, "P_inv", frame_seqlen, t_bound=t_bound)
+            gemm.module_linear(self.value_proj, v_p.flatten(2), residual=v_rows, out=v_rows)
         else:
             v_p = _se3_torch(v, prope_context, "P_inv", frame_seqlen, t_bound)
-        v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
-        if fused:
-            v_rows = v.flatten(2)
+            v = (v.flatten(2) + self.value_proj(v_p.flatten(2))).view(b, s, n, d)
 
     num_new = s
     cur_end = current_start + num_new
@@ -294,11 +298,13 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         se3_block_apply(y, prope_context, "P", frame_seqlen, out=yy[..., C:].view(b, s, n, d), t_bound=t_bound)
         write_index(kv_cache["global_end_index"], cur_end)
         write_index(kv_cache["local_end_index"], local_end)
-        return torch.nn.functional.linear(yy, *_stacked_out(self))
+        return gemm.linear(yy, *_stacked_out(self))
     attn_out = chunk_attention(q, k_slice, v_slice, rope=rope).to(x.dtype)
     write_index(kv_cache["global_end_index"], cur_end)
     write_index(kv_cache["local_end_index"], local_end)
 
+    if fused:
+        return gemm.module_linear(self.o, attn_out.flatten(2))
     out = self.o(attn_out.flatten(2))
     if prope_context is not None:
         x_p = _se3_torch(attn_out, prope_context, "P", frame_seqlen, t_bound)

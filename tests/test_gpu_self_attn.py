@@ -129,3 +129,40 @@ def test_forward_rejects_fp32_cache(cuda):
     with pytest.raises(NotImplementedError):
         mod.forward(torch.zeros(1, 60, 256, device=cuda), torch.tensor([60]), torch.tensor([[3, 4, 5]]),
                     orope.build_freqs(128), None, kv_cache=cache, current_start=0)
+
+
+def test_fp32_module_with_bf16_cache_matches_oracle(cuda):
+    """A module kept in fp32 (the 352x640 CPU configuration's dtype) on the GPU:
+    torch's fp32 projections and norms, q/k/v cast to bf16 for the cache store
+    (RoPE in rw_rope_kv_store) and the attention kernel, the output back in fp32
+    through the fp32 o projection.  Against the oracle's fp32 forward on the same
+    bf16-valued cache, within the attention tolerance; the cache bookkeeping is
+    the reference's."""
+    from reworld_b200.self_attn import install
+    mod, vals, gen = _build(torch.float32, cuda)
+    install([type("Blk", (), {"self_attn": mod})()])
+    k0, v0, x, _ = gi.self_attn_inputs(gen, torch.float32, False)
+    f, h, w = gi.SELF_ATTN_GRID
+    ct = f * h * w
+    n0 = gi.SELF_ATTN_CACHED * ct
+    cap = (gi.SELF_ATTN_CACHED + 2) * ct
+    H = gi.SELF_ATTN_HEADS
+    k0b, v0b = k0.to(torch.bfloat16), v0.to(torch.bfloat16)
+    cache = {"k": torch.zeros(1, cap, H, 128, dtype=torch.bfloat16, device=cuda),
+             "v": torch.zeros(1, cap, H, 128, dtype=torch.bfloat16, device=cuda),
+             "global_end_index": torch.tensor([n0], device=cuda), "local_end_index": torch.tensor([n0], device=cuda)}
+    cache["k"][:, :n0], cache["v"][:, :n0] = k0b.to(cuda), v0b.to(cuda)
+    freqs = orope.build_freqs(128, gi.ROPE_SCALE_H, gi.ROPE_SCALE_W)
+    with torch.no_grad():
+        y = mod.forward(x.to(cuda), torch.tensor([ct]), torch.tensor([[f, h, w]]), freqs, None, kv_cache=cache,
+                        current_start=n0)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32
+    assert [int(cache["global_end_index"]), int(cache["local_end_index"])] == [n0 + ct, n0 + ct]
+    W = {n: t.float() for n, t in vals.items()}
+    kc = {"k": torch.zeros(1, cap, H, 128), "v": torch.zeros(1, cap, H, 128),
+          "global_end_index": torch.tensor([n0]), "local_end_index": torch.tensor([n0])}
+    kc["k"][:, :n0], kc["v"][:, :n0] = k0b.float(), v0b.float()
+    y_ref, _ = osa.prop_self_attn_forward(W, x, (f, h, w), freqs, kc, n0, num_heads=H)
+    err = (y.cpu() - y_ref).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3, (err.max().item(), err.mean().item())
