@@ -313,14 +313,23 @@ int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, 
  * Requirements: bf16 row-major operands with 16-byte aligned bases, row strides
  * (elements) multiples of 8 with lda, ldb >= K, ldc, ldr >= N; K a multiple of
  * 64 and N of 128 (RW_ERR_UNSUPPORTED otherwise); bias (when used) 16-byte
- * aligned. */
+ * aligned.  workspace (device memory, 16-byte aligned, rw_gemm_workspace_bytes()
+ * bytes, ZEROED before its first use; each call leaves it ready for the next)
+ * lets the tiles of a last, partial round be shared among all CTA pairs by
+ * k-blocks, their partial sums meeting in the workspace; with workspace == NULL
+ * (or too small) those tiles run whole, same results up to fp32 summation order.
+ * Calls that share a workspace must not overlap on the GPU. */
 #define RW_GEMM_EPI_NONE 0
 #define RW_GEMM_EPI_BIAS 1
 #define RW_GEMM_EPI_BIAS_GELU 2
 #define RW_GEMM_EPI_BIAS_RESIDUAL 3
 int rw_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, const void* bias, const void* R,
-                 long long ldr, void* C, long long ldc, int M, int N, int K, int epilogue, int* status,
-                 void* stream);
+                 long long ldr, void* C, long long ldc, int M, int N, int K, int epilogue, void* workspace,
+                 long long workspace_bytes, int* status, void* stream);
+
+/* Workspace bytes rw_gemm_bf16 uses for this shape on the current device (0 when
+ * the tiles fill whole rounds). */
+long long rw_gemm_workspace_bytes(int M, int N, int K);
 
 /* Human-readable text of an RW_ERR_* code. */
 const char* rw_error_string(int code);

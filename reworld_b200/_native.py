@@ -68,7 +68,8 @@ _SIGNATURES = {
     "rw_sp_attn_fwd": (c_int, [c_vp] * 3 + [c_int] * 4 + [c_ll] * 6 + [c_vp] + [c_int] * 3
                        + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
     "rw_gemm_bf16": (c_int, [c_vp, c_ll, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_ll, c_int, c_int, c_int, c_int, c_vp,
-                             c_vp]),
+                             c_ll, c_vp, c_vp]),
+    "rw_gemm_workspace_bytes": (c_ll, [c_int, c_int, c_int]),
     "rw_error_string": (ctypes.c_char_p, [c_int]),
     "rw_abi_version": (c_int, []),
 }

@@ -146,6 +146,14 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, const void* s
       : "memory");
 }
 
+// 2-D tiled store shared -> global (rows and columns outside the tensor are clipped).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 template <int N>

@@ -71,6 +71,21 @@ inline int make_bf16_2d_map(CUtensorMap* m, const void* ptr, long long rows, lon
   return r == CUDA_SUCCESS ? 0 : -4;
 }
 
+// Row-major bf16 matrix [rows, cols] (row stride ld) for TMA stores of 32 x 32 boxes
+// (64-byte rows, 64-byte swizzle); writes outside the matrix are clipped.
+inline int make_bf16_2d_store_map(CUtensorMap* m, const void* ptr, long long rows, long long cols, long long ld) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return -4;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -4;
+}
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 // Host threads may race here: the attribute call is idempotent and the mask is
 // atomic, so a second thread at worst repeats the call.

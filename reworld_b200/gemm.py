@@ -17,6 +17,22 @@ from ._native import c_vp
 
 EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL = 0, 1, 2, 3
 
+_workspaces = {}
+
+
+def _workspace(device, nbytes):
+    """Per-device workspace of the GEMM's shared last round: zeroed once when
+    (re)allocated; every call leaves its flags at zero again.  Calls on one device
+    are stream-ordered on the current stream, so they never overlap on it."""
+    if nbytes <= 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = ws
+    return ws
+
 
 def _rows(t, name):
     """[..., n] tensor -> (2-D view [rows, n], row stride) without copying."""
@@ -74,9 +90,11 @@ def linear(x, weight, bias=None, gelu=False, residual=None, out=None):
     lib = _native.lib()
     with torch.cuda.device(x.device):
         st = _native.status_tensor(x.device)
+        ws = _workspace(x.device, lib.rw_gemm_workspace_bytes(M, N, K))
         code = lib.rw_gemm_bf16(c_vp(a.data_ptr()), lda, c_vp(w.data_ptr()), ldb, bptr, rptr, ldr,
-                                c_vp(c.data_ptr()), ldc, M, N, K, epi, c_vp(st.data_ptr()),
-                                _native.stream_ptr(x.device))
+                                c_vp(c.data_ptr()), ldc, M, N, K, epi,
+                                c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+                                c_vp(st.data_ptr()), _native.stream_ptr(x.device))
     _native.check(code, "rw_gemm_bf16")
     return out
 

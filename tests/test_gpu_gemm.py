@@ -15,6 +15,7 @@ SHAPES = [
     (2640, 14336, 3072, "gelu"), (2640, 3072, 14336, "bias"),
     (1, 128, 64, "none"), (7, 256, 64, "bias"), (300, 384, 192, "gelu"), (257, 640, 128, "residual"),
     (513, 128, 1024, "none"), (5000, 512, 256, "bias"), (660, 9216, 3072, "bias"),
+    (3000, 2560, 448, "gelu"), (3000, 2560, 448, "residual"),
 ]
 
 
@@ -105,3 +106,48 @@ def test_gemm_rejects_unsupported_shapes(cuda):
         linear(x, torch.zeros(100, 64, dtype=torch.bfloat16, device=cuda))      # N not a multiple of 128
     with pytest.raises(ValueError):
         linear(x.float(), torch.zeros(128, 64, device=cuda))
+
+
+def _raw(lib, x, w, b, out, ws, epi=1):
+    import ctypes
+    from reworld_b200 import _native
+    M, K = x.shape
+    N = w.shape[0]
+    st = _native.status_tensor(x.device)
+    return lib.rw_gemm_bf16(ctypes.c_void_p(x.data_ptr()), K, ctypes.c_void_p(w.data_ptr()), K,
+                            ctypes.c_void_p(b.data_ptr()), None, 0, ctypes.c_void_p(out.data_ptr()), N, M, N, K, epi,
+                            ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+                            ws.numel() if ws is not None else 0, ctypes.c_void_p(st.data_ptr()),
+                            _native.stream_ptr(x.device))
+
+
+@pytest.mark.parametrize("M,N,K", [(2640, 3072, 3072), (2640, 9216, 3072), (3000, 2560, 448)])
+def test_shared_last_round_matches_whole_tiles(cuda, M, N, K):
+    """The last, partial round shared out among all CTA pairs by k-blocks (partial
+    sums meeting in the workspace) against the same GEMM with every tile run whole
+    (no workspace): equal up to fp32 summation order, on three calls in a row (the
+    workspace's ready flags are reset by each call), flags zero afterwards."""
+    from reworld_b200 import _native
+    lib = _native.lib()
+    need = lib.rw_gemm_workspace_bytes(M, N, K)
+    assert need > 0                                   # these shapes leave a partial last round
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    for call in range(3):
+        x = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(N, generator=g, device=cuda) * 0.1).to(torch.bfloat16)
+        whole = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+        shared = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+        assert _raw(lib, x, w, b, whole, None) == 0
+        assert _raw(lib, x, w, b, shared, ws) == 0
+        torch.cuda.synchronize()
+        ref = x.float() @ w.float().T + b.float()
+        acc_err = 2.0 ** -18 * (x.float().abs() @ w.float().abs().T)
+        for out in (whole, shared):
+            assert torch.isfinite(out.float()).all()
+            assert bool(((out.float() - ref).abs() <= _ulp(ref) + acc_err).all()), call
+        assert (whole == shared).float().mean().item() > 0.95
+    flags = ws[-4096:].view(torch.int32)
+    assert not flags.any()
+    _native.check_status(cuda)
