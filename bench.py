@@ -186,6 +186,7 @@ class Rollout:
         self.frame_ctx = torch.from_numpy(np.stack(frames)).to(device).unsqueeze(0)
         self.launches = 0
         self.flops_all = 0.0          # attention FLOPs of all heads issued so far (whole job)
+        self.host_issue_s = []        # host time to enqueue each forward (30 layers of launches)
         self._split_cache = {}
         self.attn_events = []
 
@@ -257,7 +258,9 @@ class Rollout:
 
     def step(self, time_attn=False):
         for _ in range(FORWARDS_PER_CHUNK):
+            t0 = time.perf_counter()
             self.forward(time_attn)
+            self.host_issue_s.append(time.perf_counter() - t0)
         self.bank_update()
 
 
@@ -285,6 +288,7 @@ def run_gpu(args):
         dist.barrier()
     launches0 = ro.launches
     ro.attn_events.clear()
+    ro.host_issue_s.clear()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         torch.cuda.synchronize()
@@ -298,6 +302,7 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
     ms = e0.elapsed_time(e1) / args.steps
+    host_issue_ms = 1e3 * statistics.median(ro.host_issue_s)
     launches = (ro.launches - launches0) // args.steps
     attn_ms = [a.elapsed_time(b) for a, b, _ in ro.attn_events]
     attn_lk = [lk for _, _, lk in ro.attn_events]
@@ -332,6 +337,7 @@ def run_gpu(args):
                        "parallelism": f"ulysses{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (12.5 GB of caches + 1.5 GB activations per step)"},
             "ms_per_forward": round(ms_max / FORWARDS_PER_CHUNK, 3),
+            "host_issue_ms_per_forward": round(host_issue_ms, 3),
             "chunks_per_s": round(1000.0 / ms_max, 3),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
                          "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
