@@ -646,7 +646,63 @@ def gpu_side_baselines(ro, dev):
     out["block_ffn"] = ffn_measure(dev, timeit)
     out["gemm"] = gemm_ab(dev)
     out["dropin_layer"] = dropin_layer_measure(ro, dev)
+    out["stress_b4"] = stress_measure(dev)
     return out
+
+
+def stress_measure(dev, calls=4):
+    """The stress configuration's per-layer pieces that one GPU can hold: four
+    rollouts (batch 4) of 2640 queries over the 24-chunk budget split by the
+    pipeline (1 sink + 7 recent + 16 landmarks = 63360 keys; 66000 with the chunk
+    itself), at 24 heads and at the 3 heads one rank holds under 8-way Ulysses;
+    and the bank decision (eviction + top-16 retrieval) of a full 120-entry bank.
+    The whole 8-GPU rollout (a 120-entry bank of 4 rollouts is 467 GB) is not
+    run here."""
+    from reworld_b200 import chunk_attention
+    from reworld_b200.landmark import LandmarkBankStack, budget_split
+    from reworld_b200.poses import random_walk
+    sp = budget_split(24, 1, 7, 120, "v15b")
+    res = {"split": {"n_sink": sp.n_sink, "recent_w": sp.recent_w, "n_landmark": sp.n_landmark, "K": sp.K}}
+    g = torch.Generator(device=dev).manual_seed(21)
+    for lk in (sp.budget * CT, (sp.budget + 1) * CT):
+        for heads in (HEADS, HEADS // 8):
+            q = torch.randn(4, CT, heads, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+            k = torch.randn(4, lk, heads, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+            v = torch.randn(4, lk, heads, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+            o = torch.empty_like(q)
+            for _ in range(2):
+                chunk_attention(q, k, v, out=o)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(calls):
+                chunk_attention(q, k, v, out=o)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / calls
+            res[f"attn_b4_lk{lk}_h{heads}"] = {"ms": round(ms, 4),
+                                               "tflops": round(4 * attn_flops(CT, lk, heads) / ms / 1e9, 1)}
+            del q, k, v, o
+    # bank decisions of a 120-entry bank (tiny chunks: the decision cost does not depend on them)
+    st = LandmarkBankStack.from_budget(16, 1, 1, HEAD_DIM, 24, 1, 7, 120, device=dev)
+    src = torch.zeros(1, 16, 1, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    cap = torch.zeros(1, 25 * 16, 1, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    poses = random_walk(200, seed=8, revisit_every=8)
+    times = []
+    for c in range(len(poses)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        R = st.add_chunk_from([src[0]], [src[0]], poses[c], poses[c])
+        e1.record()
+        torch.cuda.synchronize()
+        if len(st.bank) == st.K:
+            times.append(e0.elapsed_time(e1))
+        st.write_into_caches([cap], [cap], R)
+    res["bank120_decision_ms"] = round(statistics.median(times), 4) if times else None
+    res["bank120_retrieved"] = len(R)
+    res["note"] = ("batch 4 x 24 heads is the whole stress layer on one GPU; 3 heads is one rank's share at "
+                   "8 GPUs; decision time = pack + rw_bank_step + host readback of one chunk, full bank")
+    return res
 
 
 def gemm_ab(dev, reps=9, calls=8, n_inputs=3):

@@ -78,6 +78,29 @@ def se3_mats(prope_context, mode, n_frames, dtype, t_bound=False):
     return ctx.float().contiguous()
 
 
+# The frames' matrices depend only on the camera context, not on the layer: every
+# layer of a forward reuses the ones the first layer formed.  id(context) -> (weak
+# reference, version counter, {(mode, frames, dtype, bound, device): matrices}).
+_MATS_CACHE = {}
+
+
+def _cached_mats(prope_context, mode, n_frames, dtype, t_bound, device):
+    ver = _version(prope_context)
+    key = (mode, n_frames, dtype, bool(t_bound), str(device))
+    ent = _MATS_CACHE.get(id(prope_context))
+    if ver is None or ent is None or ent[0]() is not prope_context or ent[1] != ver:
+        if ver is None:
+            return se3_mats(prope_context, mode, n_frames, dtype, t_bound).to(device)
+        k = id(prope_context)
+        ent = (weakref.ref(prope_context, lambda _r, k=k: _MATS_CACHE.pop(k, None)), ver, {})
+        _MATS_CACHE[k] = ent
+    mats = ent[2].get(key)
+    if mats is None:
+        mats = se3_mats(prope_context, mode, n_frames, dtype, t_bound).to(device)
+        ent[2][key] = mats
+    return mats
+
+
 def se3_block_apply(x, prope_context, mode, frame_seqlen, out=None, t_bound=False):
     """Block-diagonal 4x4 transform over head_dim per frame (action_model.py:84-114)
     with one rw_se3_block_apply launch.  x: bf16 [B, L, H, 128] on the GPU (any
@@ -88,7 +111,7 @@ def se3_block_apply(x, prope_context, mode, frame_seqlen, out=None, t_bound=Fals
         raise ValueError("se3_block_apply runs on bf16 CUDA tensors")
     if L % frame_seqlen != 0:
         raise ValueError(f"{L} tokens are not whole frames of {frame_seqlen}")
-    mats = se3_mats(prope_context, mode, L // frame_seqlen, x.dtype, t_bound).to(x.device)
+    mats = _cached_mats(prope_context, mode, L // frame_seqlen, x.dtype, t_bound, x.device)
     if out is None:
         out = torch.empty((B, L, H, D), dtype=torch.bfloat16, device=x.device)
     lib = _native.lib()
@@ -140,8 +163,14 @@ def _stacked_out(self):
     bo, bp = self.o.bias, self.prope_proj.bias
     if bo is None and bp is None:
         return W, None
-    bias = (bo.detach() if bo is not None else 0) + (bp.detach() if bp is not None else 0)
-    return W, bias
+    # b_o + b_prope, formed again only when either bias tensor changed (in place or replaced)
+    key = tuple((t.data_ptr(), _version(t)) if t is not None else None for t in (bo, bp))
+    cached = getattr(self, "_rw_bout", None)
+    if cached is None or cached[0] != key or None in (k[1] for k in key if k is not None):
+        bias = (bo.detach() if bo is not None else 0) + (bp.detach() if bp is not None else 0)
+        self._rw_bout = (key, bias)
+        return W, bias
+    return W, cached[1]
 
 
 # Host mirrors of the kv_cache index tensors this module wrote last:
