@@ -87,13 +87,13 @@ struct Work {
   int tile, kb0, kb1, kind, q_lo;
 };
 
-// The pairs' work: floor(T / Np) rounds of whole tiles (pair p: tiles p, p + Np, ...);
-// then, with the split on, the remaining R tiles' R * KB k-blocks form one sequence
+// The pairs' work: floor(T / Np) rounds of whole tiles (pair p: tiles p, p + Np, ...)
+// and, with the split on, the remaining R tiles' R * KB k-blocks as one sequence
 // (tile-major) of which pair p takes [U p / Np, U (p + 1) / Np), U = R * KB: at most
-// one tile's end (its final part) and the next tile's start (a partial part).  The
-// partial part runs first, so a pair waiting on earlier pairs' partials never holds
-// up a partial that another pair waits for.  Without the split the tail tiles run
-// whole in one more round.
+// one tile's end (its final part) and the next tile's start (a partial part).  A
+// pair runs its partial part first, then its final part, then its whole tiles, so a
+// pair waiting on earlier pairs' partials never holds up a partial that another pair
+// waits for.  Without the split the tail tiles run whole in one more round.
 struct WorkIter {
   int pair, Np, KB, tiles, whole, k, n_tail;
   Work tail0, tail1;  // the tail items in order (kept out of an indexed array: no local memory)
@@ -134,15 +134,17 @@ struct WorkIter {
     while (q > 0 && U * q / Np > u) --q;
     return q;
   }
+  // The tail items come first: every partial is published early, the finalising
+  // epilogues overlap the whole tiles' main loops, and all pairs end on a whole tile.
   __device__ bool next(Work& w) {
-    if (k < whole) {
-      w = Work{pair + k * Np, 0, KB, 0, 0};
+    if (k < n_tail) {
+      w = k == 0 ? tail0 : tail1;
       ++k;
       return true;
     }
-    const int j = k - whole;
-    if (j >= n_tail) return false;
-    w = j == 0 ? tail0 : tail1;
+    const int j = k - n_tail;
+    if (j >= whole) return false;
+    w = Work{pair + j * Np, 0, KB, 0, 0};
     ++k;
     return true;
   }
