@@ -248,6 +248,27 @@ int rw_bank_step(rw_bank_state_t* state, int K, int protect_n, int admit, const 
 int rw_a2a_pack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
 int rw_a2a_unpack(const void* src, void* dst, int B, int Ls, int H, int D, int P, void* stream);
 
+/* Cross-rank ordering carried by a sequence-parallel kernel itself, in place of a
+ * separate barrier launch on each side of an exchange.  sig_ptrs: DEVICE array of
+ * P pointers to each rank's int32 signal array (symmetric memory, zeroed before
+ * first use).  wait_epoch > 0: before touching data other ranks write, the kernel
+ * waits (bounded: RW_STATUS_TIMEOUT_PEER in *status after timeout_ms) until this
+ * rank's entries wait_slot .. wait_slot + P - 1 hold at least wait_epoch.
+ * signal_epoch > 0: once every CTA of the call has finished, its stores (peer
+ * memory included) visible system-wide, the last CTA writes signal_epoch into
+ * entry signal_slot + rank of every rank's array; counter is this rank's int32
+ * completion counter for the call (DEVICE, zero before its first use; every
+ * completed call leaves it at zero again).  Epochs increase from call to call,
+ * the same sequence on every rank. */
+typedef struct rw_sp_sync {
+  const unsigned long long* sig_ptrs;
+  int* counter;
+  int P, rank;
+  int wait_slot, wait_epoch;
+  int signal_slot, signal_epoch;
+  int timeout_ms, pad;
+} rw_sp_sync_t;
+
 /* Ulysses exchanges over peer memory (one sequence, B = 1), the layout
  * transform fused in; q_dst / ck_dst / cv_dst / out_dst are DEVICE arrays of P
  * pointers (this rank's entry is its own buffer, the others are peer-mapped).
@@ -260,14 +281,22 @@ int rw_a2a_unpack(const void* src, void* dst, int B, int Ls, int H, int D, int P
  * cache write of wan_5b/modules/action_model.py:265-292 on the receiving side.
  * rw_sp_scatter_out: o [P*Ls, H/P, 128] (this rank's heads, whole chunk) ->
  * out_dst[p] ([Ls, H, 128]) rows of rank p, heads [r*H/P, (r+1)*H/P); replaces
- * the head->seq all_to_all of ulysses.py:54.  Cross-rank completion is the
- * caller's barrier after each call. */
+ * the head->seq all_to_all of ulysses.py:54.  Cross-rank completion: `sync`
+ * (optional, NULL = the caller's barrier) waits before the first store and
+ * signals once the call's stores are visible to every rank. */
 int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, long long q_sl, long long q_sh, long long k_sl,
                       long long k_sh, long long v_sl, long long v_sh, const unsigned long long* q_dst,
                       const unsigned long long* ck_dst, const unsigned long long* cv_dst, int Ls, int H, int D,
-                      int P, int rank, int dst_start, int cap, const rw_rope_t* rope, void* stream);
+                      int P, int rank, int dst_start, int cap, const rw_rope_t* rope, const rw_sp_sync_t* sync,
+                      int* status, void* stream);
 int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P, int rank,
                       void* stream);
+
+
+/* rw_sp_wait: a kernel that only waits (the wait half of *sync), for a stream
+ * that must see other ranks' signalled work before it continues, e.g. the
+ * consumer of a layer's exchanged output. */
+int rw_sp_wait(const rw_sp_sync_t* sync, int* status, void* stream);
 
 /* rw_sp_barrier: stream-ordered barrier of the P ranks of a sequence-parallel
  * group over peer memory.  sig_ptrs: DEVICE array of P pointers to each rank's
@@ -290,11 +319,15 @@ int rw_sp_barrier(const unsigned long long* sig_ptrs, int slot_base, int P, int 
  * row t % (Lq/P), head rank*Hp + hl, through peer pointers (DEVICE array of P
  * pointers).  Same attention as rw_attn_fwd (workspace, rope, status alike);
  * replaces the attention call of ulysses.py:44-52 together with the head->seq
- * all_to_all of ulysses.py:54.  Cross-rank completion is the caller's barrier. */
+ * all_to_all of ulysses.py:54.  Cross-rank completion: `sync` (optional, NULL =
+ * the caller's barriers) makes every CTA wait, before its first load, for the
+ * ranks' scatters into q / k / v, and signals once every output row (of the
+ * merge kernel too, when the key split needs one) has reached its owner. */
 int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, int Hp, int D, long long q_sl,
                    long long q_sh, long long k_sl, long long k_sh, long long v_sl, long long v_sh,
                    const unsigned long long* out_ptrs, int P, int rank, int H, float softmax_scale,
-                   const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status, void* stream);
+                   const rw_rope_t* rope, void* workspace, long long workspace_bytes, const rw_sp_sync_t* sync,
+                   int* status, void* stream);
 
 /* Dense bf16 GEMM on CTA pairs (2-SM tcgen05.mma, TMA-fed stages, fp32
  * accumulation in tensor memory):

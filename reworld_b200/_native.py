@@ -41,6 +41,13 @@ class RwRope(ctypes.Structure):
     ]
 
 
+class RwSpSync(ctypes.Structure):
+    """rw_sp_sync_t: cross-rank ordering carried by a sequence-parallel kernel."""
+    _fields_ = [("sig_ptrs", c_vp), ("counter", c_vp), ("P", c_int), ("rank", c_int), ("wait_slot", c_int),
+                ("wait_epoch", c_int), ("signal_slot", c_int), ("signal_epoch", c_int), ("timeout_ms", c_int),
+                ("pad", c_int)]
+
+
 class RwCopyDesc(ctypes.Structure):
     _fields_ = [("src", c_vp), ("dst", c_vp), ("nbytes", c_ll)]
 
@@ -62,11 +69,12 @@ _SIGNATURES = {
     "rw_a2a_pack": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "rw_a2a_unpack": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "rw_sp_scatter_qkv": (c_int, [c_vp, c_vp, c_vp] + [c_ll] * 6 + [c_vp, c_vp, c_vp] + [c_int] * 7
-                          + [ctypes.POINTER(RwRope), c_vp]),
+                          + [ctypes.POINTER(RwRope), ctypes.POINTER(RwSpSync), c_vp, c_vp]),
+    "rw_sp_wait": (c_int, [ctypes.POINTER(RwSpSync), c_vp, c_vp]),
     "rw_sp_scatter_out": (c_int, [c_vp, c_vp] + [c_int] * 5 + [c_vp]),
     "rw_sp_barrier": (c_int, [c_vp] + [c_int] * 5 + [c_vp, c_vp]),
     "rw_sp_attn_fwd": (c_int, [c_vp] * 3 + [c_int] * 4 + [c_ll] * 6 + [c_vp] + [c_int] * 3
-                       + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
+                       + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, ctypes.POINTER(RwSpSync), c_vp, c_vp]),
     "rw_gemm_bf16": (c_int, [c_vp, c_ll, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_ll, c_int, c_int, c_int, c_int, c_vp,
                              c_ll, c_vp, c_vp]),
     "rw_gemm_workspace_bytes": (c_ll, [c_int, c_int, c_int]),
@@ -74,7 +82,7 @@ _SIGNATURES = {
     "rw_abi_version": (c_int, []),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 _lib = None
 
 

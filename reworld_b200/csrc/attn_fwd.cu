@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
+#include "sp_sync.cuh"
 
 namespace rw {
 namespace attn {
@@ -48,10 +49,12 @@ __host__ __device__ inline long long share_start(long long T, int Np, int p) { r
 // rank t / peer_Ls, row t % peer_Ls, head peer_h0 + h of its [Ls, peer_H, 128]
 // buffer instead of `out`.
 constexpr int COMBINE_COLS = 32;
-__global__ void __launch_bounds__(128)
-    combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
-                   long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
-                   const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0) {
+// One block's share of combine_kernel (returns early for rows and units with nothing to merge).
+__device__ __forceinline__ void combine_unit(const float* __restrict__ scratch, uint8_t* __restrict__ out,
+                                             long long o_sb, long long o_sl, long long o_sh, int Lq, int H, int nqp,
+                                             int n_kv, int U, int Np, float scale_log2,
+                                             const unsigned long long* __restrict__ peer_ptrs, int peer_Ls,
+                                             int peer_H, int peer_h0) {
   const int base = (U / Np) * Np;                  // units of the waves (written whole)
   const int unit = base + (int)blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
   const long long T = (long long)(U - base) * n_kv;
@@ -103,6 +106,17 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+__global__ void __launch_bounds__(128)
+    combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
+                   long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
+                   const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0,
+                   const __grid_constant__ rw_sp_sync_t sync, int sync_signal) {
+  combine_unit(scratch, out, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, U, Np, scale_log2, peer_ptrs, peer_Ls, peer_H,
+               peer_h0);
+  if (sync_signal) sp_signal_done(sync);  // every merged row is at its owner rank
+}
+
+
 // Work shape of one call: Np pairs; `shared` when pairs share tail units
 // (workspace and merge needed; tail = the units after whole waves).
 struct Work {
@@ -131,7 +145,8 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
-           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream);
+           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, const rw_sp_sync_t* sync,
+           bool sync_signal, cudaStream_t stream);
 }  // namespace pair
 }  // namespace rw
 
@@ -149,6 +164,7 @@ namespace {
 struct PeerArgs {
   const unsigned long long* ptrs;  // nullptr: output to o
   int Ls, H, h0;
+  const rw_sp_sync_t* sync;        // nullptr: the caller orders the exchanges
 };
 
 int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq, int Lk, int H, int D, long long q_sb,
@@ -175,15 +191,19 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
   attn::Work wk = attn::work_for(units, n_kv, pair::resident_pairs(), workspace != nullptr);
   if (wk.shared && (workspace_bytes < attn::workspace_bytes_for(wk) || !aligned16(workspace)))
     wk = attn::work_for(units, n_kv, 0, false);
+  // with a sync record the signal comes from the last kernel that writes output rows
   const int rc = pair::launch(q, k, v, o, B, Lq, Lk, H, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb,
                               o_sl, o_sh, scale_log2, rope, status, wk.shared ? (float*)workspace : nullptr, nqp,
-                              units, wk.Np, peer.ptrs, peer.Ls, peer.H, peer.h0, (cudaStream_t)stream);
+                              units, wk.Np, peer.ptrs, peer.Ls, peer.H, peer.h0, peer.sync, !wk.shared,
+                              (cudaStream_t)stream);
   if (rc != RW_OK) return rc;
   if (wk.shared) {
     const int tail_units = units - (units / wk.Np) * wk.Np;
+    rw_sp_sync_t none{};
+    const bool sig = peer.sync != nullptr && peer.sync->signal_epoch > 0;
     attn::combine_kernel<<<dim3(tail_units, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
         (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, units, wk.Np, scale_log2,
-        peer.ptrs, peer.Ls, peer.H, peer.h0);
+        peer.ptrs, peer.Ls, peer.H, peer.h0, sig ? *peer.sync : none, sig ? 1 : 0);
     if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
   }
   return RW_OK;
@@ -197,19 +217,21 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
                            long long o_sl, long long o_sh, float softmax_scale, const rw_rope_t* rope,
                            void* workspace, long long workspace_bytes, int* status, void* stream) {
   return attn_run(q, k, v, o, B, Lq, Lk, H, D, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb, o_sl,
-                  o_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream, PeerArgs{nullptr, 0, 0, 0});
+                  o_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
+                  PeerArgs{nullptr, 0, 0, 0, nullptr});
 }
 
 extern "C" int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, int Hp, int D,
                               long long q_sl, long long q_sh, long long k_sl, long long k_sh, long long v_sl,
                               long long v_sh, const unsigned long long* out_ptrs, int P, int rank, int H,
                               float softmax_scale, const rw_rope_t* rope, void* workspace,
-                              long long workspace_bytes, int* status, void* stream) {
+                              long long workspace_bytes, const rw_sp_sync_t* sync, int* status, void* stream) {
   if (out_ptrs == nullptr || !q) return RW_ERR_INVALID_ARG;
   if (P < 1 || rank < 0 || rank >= P || H < 1 || Hp < 1 || H != Hp * P || Lq < 1 || (Lq % P) != 0)
     return RW_ERR_INVALID_ARG;
+  if (sync != nullptr && (!sp_sync_ok(*sync) || sync->P != P || sync->rank != rank)) return RW_ERR_INVALID_ARG;
   // o is never written in this mode; q's layout stands in for it in the unused output map
   return attn_run(q, k, v, const_cast<void*>(q), 1, Lq, Lk, Hp, D, 0, q_sl, q_sh, 0, k_sl, k_sh, 0, v_sl, v_sh, 0,
                   q_sl, q_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
-                  PeerArgs{out_ptrs, Lq / P, H, rank * Hp});
+                  PeerArgs{out_ptrs, Lq / P, H, rank * Hp, sync});
 }

@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
+#include "sp_sync.cuh"
 
 namespace rw {
 namespace pair {
@@ -99,6 +100,9 @@ struct Params {
   int* status;
   float* scratch;
   PeerOut peer;  // peer.ptrs == nullptr: output through tm_o (local); else rows go to their owner ranks
+  int sync_wait;    // 1: every CTA's producer waits for the ranks' scatters before its first load
+  int sync_signal;  // 1: the last CTA to finish signals the ranks (no merge kernel follows)
+  rw_sp_sync_t sync;
 };
 
 struct __align__(8) Barriers {
@@ -292,6 +296,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_o);
     }
+    if (p.sync_wait && lane == 0 && !sp_wait_peers(p.sync, p.status, &sb.abort_flag) && !aborted()) {
+      // the ranks' q / k / v did not arrive in time: stop both CTAs of the pair
+      sb.abort_flag = 1;
+      st_shared_cluster_u32(cx.peer_abort, 1u);
+    }
+    __syncwarp();
     SegIter it(p, pair_id, n_kv_all);
     Seg sg;
     int J0 = 0, segi = 0;  // key tiles and segments of this pair before the current one
@@ -693,6 +703,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem, 512);
   }
+  if (p.sync_signal) sp_signal_done(p.sync);  // every output row is at its owner rank
 }
 
 }  // namespace pair
@@ -738,7 +749,8 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
-           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, cudaStream_t stream) {
+           const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, const rw_sp_sync_t* sync,
+           bool sync_signal, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, mo;
   if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, HD, q_sb, q_sl, q_sh, BM) ||
       make_bf16_bl_hd_map(&mk, k, B, Lk, H, HD, k_sb, k_sl, k_sh, BN / 2) ||
@@ -763,6 +775,13 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   if (rope != nullptr) {
     prm.rope = *rope;
     prm.rope_on = 1;
+  }
+  prm.sync_wait = 0;
+  prm.sync_signal = 0;
+  if (sync != nullptr) {
+    prm.sync = *sync;
+    prm.sync_wait = sync->wait_epoch > 0 ? 1 : 0;
+    prm.sync_signal = sync_signal && sync->signal_epoch > 0 ? 1 : 0;
   }
   if (Np < 1 || U < 1 || 2LL * Np > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
   if (U % Np != 0 && (long long)(U % Np) * ((Lk + BN - 1) / BN) < Np) return RW_ERR_INVALID_ARG;  // empty tail shares

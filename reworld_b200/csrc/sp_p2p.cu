@@ -18,11 +18,13 @@
 // pointers; no multicast), so no packed staging buffer, no collective library
 // call and no separate cache-write kernel are needed.  rw_sp_scatter_out sends
 // the attention output o[t][hl] (t in [0, P*Ls)) back to rank p = t / Ls as
-// out_dst[p][t % Ls][r*Hp + hl].  Completion across ranks is signalled by the
-// caller (a stream-ordered barrier after each scatter).
+// out_dst[p][t % Ls][r*Hp + hl].  Completion across ranks: either the caller's
+// stream-ordered barrier after each scatter, or the scatter's own sync record
+// (sp_sync.cuh: a bounded wait before its first store, a signal from its last CTA).
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
+#include "sp_sync.cuh"
 
 namespace rw {
 namespace sp {
@@ -38,6 +40,9 @@ struct ScatterQKV {
   int Ls, H, Hp, P, rank, dst_start;
   int rope_on;
   rw_rope_t rope;
+  int sync_on;
+  rw_sp_sync_t sync;
+  int* status;
 };
 
 constexpr int SCATTER_THREADS = 128;  // a multiple of 16 (see scatter_qkv_kernel)
@@ -47,6 +52,16 @@ constexpr int SCATTER_THREADS = 128;  // a multiple of 16 (see scatter_qkv_kerne
 // threadIdx.x mod 16 of their head, so its 4 RoPE table entries are looked up
 // once per token.
 __global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
+  __shared__ int go;
+  if (p.sync_on && p.sync.wait_epoch > 0) {
+    // the ranks' earlier reads of the buffers this scatter overwrites are done
+    if (threadIdx.x == 0) go = sp_wait_peers(p.sync, p.status, nullptr) ? 1 : 0;
+    __syncthreads();
+    if (!go) {
+      if (p.sync.signal_epoch > 0) sp_signal_done(p.sync);
+      return;
+    }
+  }
   const int nch = p.H * 16;
   const int c16 = threadIdx.x & 15;
   const long long eoff = (long long)c16 * 8;
@@ -84,6 +99,11 @@ __global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __gr
       *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv;
     }
   }
+  if (p.sync_on && p.sync.signal_epoch > 0) sp_signal_done(p.sync);
+}
+
+__global__ void __launch_bounds__(32) wait_kernel(const __grid_constant__ rw_sp_sync_t s, int* status) {
+  if (threadIdx.x == 0) sp_wait_peers(s, status, nullptr);
 }
 
 __global__ void __launch_bounds__(256)
@@ -105,14 +125,6 @@ __global__ void __launch_bounds__(256)
 }
 
 // Cross-rank barrier: thread p signals rank p and waits for rank p's signal.
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(32) barrier_kernel(const unsigned long long* __restrict__ sig_ptrs, int slot_base,
                                                      int P, int rank, int epoch, unsigned long long timeout_ns,
@@ -150,7 +162,8 @@ extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, lo
                                  long long k_sl, long long k_sh, long long v_sl, long long v_sh,
                                  const unsigned long long* q_dst, const unsigned long long* ck_dst,
                                  const unsigned long long* cv_dst, int Ls, int H, int D, int P, int rank,
-                                 int dst_start, int cap, const rw_rope_t* rope, void* stream) {
+                                 int dst_start, int cap, const rw_rope_t* rope, const rw_sp_sync_t* sync,
+                                 int* status, void* stream) {
   if (!q || !k || !v || !q_dst || !ck_dst || !cv_dst) return RW_ERR_INVALID_ARG;
   if (D != 128) return RW_ERR_UNSUPPORTED;
   if (Ls < 1 || H < 1 || P < 1 || (H % P) != 0 || rank < 0 || rank >= P || dst_start < 0) return RW_ERR_INVALID_ARG;
@@ -178,6 +191,13 @@ extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, lo
     if (!rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
     p.rope = *rope;
     p.rope_on = 1;
+  }
+  p.sync_on = 0;
+  p.status = status;
+  if (sync != nullptr) {
+    if (!sp_sync_ok(*sync) || sync->P != P || sync->rank != rank) return RW_ERR_INVALID_ARG;
+    p.sync = *sync;
+    p.sync_on = 1;
   }
   {
     int dev = 0, sms = 148;
@@ -207,5 +227,11 @@ extern "C" int rw_sp_barrier(const unsigned long long* sig_ptrs, int slot_base, 
     return RW_ERR_INVALID_ARG;
   sp::barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(sig_ptrs, slot_base, P, rank, epoch,
                                                          (unsigned long long)timeout_ms * 1000000ull, status);
+  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+}
+
+extern "C" int rw_sp_wait(const rw_sp_sync_t* sync, int* status, void* stream) {
+  if (sync == nullptr || !sp_sync_ok(*sync) || sync->wait_epoch <= 0) return RW_ERR_INVALID_ARG;
+  sp::wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*sync, status);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }

@@ -140,14 +140,26 @@ class UlyssesP2P:
     """Head-parallel cached chunk attention with the exchanges done by this
     package's kernels over peer memory (NVLink) instead of a collective library.
 
-    Per layer: rw_sp_scatter_qkv (each rank writes its sequence shard's q into
-    the owning rank's q buffer and its roped k and v straight into the owning
-    rank's KV cache), a barrier, rw_sp_attn_fwd (the chunk attention on the local
-    heads over the local, head-resident cache, whose epilogue stores every output
-    row straight into the buffer of the rank that owns the token), a barrier.  The q buffer, output buffer and all
-    layers' caches are allocated as symmetric memory so every rank holds the
-    peers' device pointers.  One sequence (B = 1), as in the streaming rollout.
+    Per layer, two launches: rw_sp_scatter_qkv (each rank writes its sequence
+    shard's q into the owning rank's q buffer and its roped k and v straight into
+    the owning rank's KV cache; its last CTA then signals every rank), and
+    rw_sp_attn_fwd (every CTA first waits, bounded, for all ranks' scatter signals,
+    then runs the chunk attention on the local heads over the local, head-resident
+    cache; its epilogue stores every output row straight into the buffer of the
+    rank that owns the token, and its last CTA — or the merge kernel's, when the
+    key split needs one — signals every rank again).  The cross-rank ordering thus
+    rides on the two kernels (no barrier launches).  The q and output buffers
+    alternate between two copies from call to call: when a rank scatters call
+    n + 2 into q copy n % 2, every rank has passed call n + 1's wait, i.e. finished
+    call n's attention, so nothing still reads that copy.  `layer(...,
+    sync_output=True)` adds a wait for every rank's output rows (rw_sp_wait) before
+    returning; a caller that reads the output later calls `finish()` first.  The q
+    buffers, output buffers, all layers' caches and the signal array are symmetric
+    memory, so every rank holds the peers' device pointers.  One sequence (B = 1),
+    as in the streaming rollout.
     """
+
+    SLOT_SCATTER, SLOT_ATTN, SLOT_BARRIER = 0, 1, 2     # signal slots, in units of P
 
     def __init__(self, group, n_layers, cap_tokens, chunk_tokens, heads, head_dim=128, device=None,
                  barrier_timeout_ms=10000):
@@ -163,9 +175,10 @@ class UlyssesP2P:
         self.timeout_ms = barrier_timeout_ms
         bf16 = torch.bfloat16
         self.caches = symm.empty(n_layers, 2, cap_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
-        self.qbuf = symm.empty(chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
-        self.obuf = symm.empty(self.Ls, heads, head_dim, dtype=bf16, device=self.device)
-        self.sig = symm.empty(2 * self.P, dtype=torch.int32, device=self.device)   # barrier signal slots
+        self.qbuf = symm.empty(2, chunk_tokens, self.Hp, head_dim, dtype=bf16, device=self.device)
+        self.obuf = symm.empty(2, self.Ls, heads, head_dim, dtype=bf16, device=self.device)
+        self.sig = symm.empty(4 * self.P, dtype=torch.int32, device=self.device)   # signal slots
+        self.counters = torch.zeros(2, dtype=torch.int32, device=self.device)     # scatter, attention
         self.caches.zero_()
         self.sig.zero_()
         torch.cuda.synchronize(self.device)   # zeroed on every rank before any peer can signal into it
@@ -179,8 +192,11 @@ class UlyssesP2P:
         base = list(self.h_c.buffer_ptrs)
         ptrs = [[[b + (l * 2 + kv) * per_tensor for b in base] for kv in range(2)] for l in range(n_layers)]
         self.cache_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)   # [layer, k/v, P]
-        self.q_ptrs = torch.tensor(list(self.h_q.buffer_ptrs), dtype=torch.int64, device=self.device)
-        self.o_ptrs = torch.tensor(list(self.h_o.buffer_ptrs), dtype=torch.int64, device=self.device)
+        qsz, osz = self.qbuf[0].numel() * 2, self.obuf[0].numel() * 2
+        self.q_ptrs = torch.tensor([[b + c * qsz for b in self.h_q.buffer_ptrs] for c in range(2)], dtype=torch.int64,
+                                   device=self.device)                             # [copy, P]
+        self.o_ptrs = torch.tensor([[b + c * osz for b in self.h_o.buffer_ptrs] for c in range(2)], dtype=torch.int64,
+                                   device=self.device)
 
     def cache_k(self, layer):
         return self.caches[layer, 0].unsqueeze(0)
@@ -188,43 +204,47 @@ class UlyssesP2P:
     def cache_v(self, layer):
         return self.caches[layer, 1].unsqueeze(0)
 
-    def scatter_qkv(self, layer, q, k, v, dst_start, rope=None):
+    def _sync(self, counter=None, wait_slot=0, wait_epoch=0, signal_slot=0, signal_epoch=0):
+        return _native.RwSpSync(c_vp(self.sig_ptrs.data_ptr()),
+                                c_vp(self.counters[counter].data_ptr()) if counter is not None else None,
+                                self.P, self.rank, wait_slot * self.P, wait_epoch, signal_slot * self.P,
+                                signal_epoch, self.timeout_ms, 0)
+
+    def scatter_qkv(self, layer, q, k, v, dst_start, rope=None, copy=0, sync=None):
         """q, k, v: [1, Ls, H, D] bf16 (this rank's tokens, all heads)."""
         import ctypes
         lib = _native.lib()
         rs = rope.struct() if rope is not None else None
+        st = _native.status_tensor(self.device)
         code = lib.rw_sp_scatter_qkv(
             c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()),
             q.stride(1), q.stride(2), k.stride(1), k.stride(2), v.stride(1), v.stride(2),
-            c_vp(self.q_ptrs.data_ptr()), c_vp(self.cache_ptrs[layer, 0].data_ptr()),
+            c_vp(self.q_ptrs[copy].data_ptr()), c_vp(self.cache_ptrs[layer, 0].data_ptr()),
             c_vp(self.cache_ptrs[layer, 1].data_ptr()), self.Ls, self.H, self.D, self.P, self.rank,
-            int(dst_start), self.cap, ctypes.byref(rs) if rs is not None else None, _native.stream_ptr(self.device))
+            int(dst_start), self.cap, ctypes.byref(rs) if rs is not None else None,
+            ctypes.byref(sync) if sync is not None else None, c_vp(st.data_ptr()), _native.stream_ptr(self.device))
         _native.check(code, "rw_sp_scatter_qkv")
 
-    def scatter_out(self, o):
-        lib = _native.lib()
-        code = lib.rw_sp_scatter_out(c_vp(o.data_ptr()), c_vp(self.o_ptrs.data_ptr()), self.L, self.H, self.D,
-                                     self.P, self.rank, _native.stream_ptr(self.device))
-        _native.check(code, "rw_sp_scatter_out")
-
-    def barrier(self, slot_base):
+    def barrier(self, slot_base=None):
         """Stream-ordered barrier of the group over the peer-mapped signal array
         (rw_sp_barrier); everything each rank enqueued before it is visible to all
         ranks after it."""
+        if slot_base is None:
+            slot_base = self.SLOT_BARRIER * self.P
         lib = _native.lib()
         st = _native.status_tensor(self.device)
+        self.epoch += 1
         code = lib.rw_sp_barrier(c_vp(self.sig_ptrs.data_ptr()), slot_base, self.P, self.rank, self.epoch,
                                  self.timeout_ms, c_vp(st.data_ptr()), _native.stream_ptr(self.device))
         _native.check(code, "rw_sp_barrier")
 
-    def attend(self, layer, lk, rope=None):
+    def attend(self, layer, lk, rope=None, copy=0, sync=None):
         """Attention of this rank's heads over cache rows [0, lk) with the output
-        rows sent to their owner ranks' output buffers (complete after the next
-        barrier)."""
+        rows sent to their owner ranks' output buffers."""
         import ctypes
         from .attention import _workspace
         lib = _native.lib()
-        q = self.qbuf
+        q = self.qbuf[copy]
         kc, vc = self.caches[layer, 0], self.caches[layer, 1]
         rs = rope.struct() if rope is not None else None
         st = _native.status_tensor(self.device)
@@ -232,26 +252,48 @@ class UlyssesP2P:
         code = lib.rw_sp_attn_fwd(
             c_vp(q.data_ptr()), c_vp(kc.data_ptr()), c_vp(vc.data_ptr()), self.L, lk, self.Hp, self.D,
             q.stride(0), q.stride(1), kc.stride(0), kc.stride(1), vc.stride(0), vc.stride(1),
-            c_vp(self.o_ptrs.data_ptr()), self.P, self.rank, self.H, 1.0 / math.sqrt(self.D),
+            c_vp(self.o_ptrs[copy].data_ptr()), self.P, self.rank, self.H, 1.0 / math.sqrt(self.D),
             ctypes.byref(rs) if rs is not None else None,
             c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
-            c_vp(st.data_ptr()), _native.stream_ptr(self.device))
+            ctypes.byref(sync) if sync is not None else None, c_vp(st.data_ptr()), _native.stream_ptr(self.device))
         _native.check(code, "rw_sp_attn_fwd")
 
-    def layer(self, layer, q, k, v, dst_start, rope=None, attn_events=None):
+    def finish(self):
+        """Waits on this rank's stream until every rank's output rows of the last
+        layer() call have arrived (rw_sp_wait)."""
+        if self.epoch == 0:
+            return
+        s = self._sync(wait_slot=self.SLOT_ATTN, wait_epoch=self.epoch)
+        import ctypes
+        st = _native.status_tensor(self.device)
+        code = _native.lib().rw_sp_wait(ctypes.byref(s), c_vp(st.data_ptr()), _native.stream_ptr(self.device))
+        _native.check(code, "rw_sp_wait")
+
+    def layer(self, layer, q, k, v, dst_start, rope=None, attn_events=None, sync_output=True, scatter_events=None):
         """One layer's cached chunk attention; returns [1, Ls, H, D] (this rank's
-        tokens, all heads; valid until the next call's output exchange)."""
+        tokens, all heads), complete on return when sync_output, else after
+        finish() (valid until the call after next, which reuses its copy).
+        attn_events / scatter_events: optional CUDA event pairs recorded around the
+        attention and the scatter launches."""
         for t in (q, k, v):
             if t.dtype != torch.bfloat16 or t.shape != (1, self.Ls, self.H, self.D) or t.stride(-1) != 1:
                 raise ValueError("q, k, v must be bf16 [1, L/P, H, D] with a contiguous head dim")
         self.epoch += 1
-        self.scatter_qkv(layer, q, k, v, dst_start, rope)
-        self.barrier(0)
+        e, copy = self.epoch, self.epoch & 1
+        if scatter_events is not None:
+            scatter_events[0].record()
+        self.scatter_qkv(layer, q, k, v, dst_start, rope, copy,
+                         self._sync(counter=0, signal_slot=self.SLOT_SCATTER, signal_epoch=e))
+        if scatter_events is not None:
+            scatter_events[1].record()
         lk = dst_start + self.L
         if attn_events is not None:
             attn_events[0].record()
-        self.attend(layer, lk, rope)
+        self.attend(layer, lk, rope, copy,
+                    self._sync(counter=1, wait_slot=self.SLOT_SCATTER, wait_epoch=e, signal_slot=self.SLOT_ATTN,
+                               signal_epoch=e))
         if attn_events is not None:
             attn_events[1].record()
-        self.barrier(self.P)
-        return self.obuf.unsqueeze(0)
+        if sync_output:
+            self.finish()
+        return self.obuf[copy].unsqueeze(0)

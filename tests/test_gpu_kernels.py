@@ -242,6 +242,52 @@ def test_sp_barrier_single_rank_and_timeout(cuda):
     assert float((x * 2).sum()) == 32.0                      # context still usable
 
 
+def test_sp_sync_signal_and_wait_emulated(cuda):
+    """The sync record of the peer-memory kernels on one GPU: a scatter of rank 1 of
+    4 (owners' buffers and signal arrays local) signals, from its last CTA, epoch 7
+    into entry slot + 1 of all four signal arrays and leaves its completion counter
+    at zero; rw_sp_wait returns at once for epochs already signalled and, for a
+    rank that never signals, ends after its time limit with RW_STATUS_TIMEOUT_PEER
+    (no fault; the context stays usable)."""
+    import ctypes
+    from reworld_b200 import _native
+    from reworld_b200._native import RwSpSync, c_vp
+    P, rank, H, Ls = 4, 1, 8, 300
+    Hp = H // P
+    q, k, v = (torch.randn(Ls, H, 128, device=cuda).to(torch.bfloat16) for _ in range(3))
+    qd = [torch.zeros(P * Ls, Hp, 128, dtype=torch.bfloat16, device=cuda) for _ in range(P)]
+    cd = [torch.zeros(P * Ls, Hp, 128, dtype=torch.bfloat16, device=cuda) for _ in range(2 * P)]
+    ptrs = [torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=cuda) for ts in (qd, cd[:P], cd[P:])]
+    sig = torch.zeros(P, 16, dtype=torch.int32, device=cuda)
+    sig_ptrs = torch.tensor([sig[p].data_ptr() for p in range(P)], dtype=torch.int64, device=cuda)
+    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
+    st = torch.zeros(4, dtype=torch.int32, device=cuda)
+    lib = _native.lib()
+    sync = RwSpSync(c_vp(sig_ptrs.data_ptr()), c_vp(counter.data_ptr()), P, rank, 0, 0, 4, 7, 1000, 0)
+    code = lib.rw_sp_scatter_qkv(
+        c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()), q.stride(0), q.stride(1), k.stride(0),
+        k.stride(1), v.stride(0), v.stride(1), *(c_vp(t.data_ptr()) for t in ptrs), Ls, H, 128, P, rank, 0,
+        P * Ls, None, ctypes.byref(sync), c_vp(st.data_ptr()), _native.stream_ptr(cuda))
+    _native.check(code, "rw_sp_scatter_qkv")
+    torch.cuda.synchronize()
+    assert all(int(sig[p, 4 + rank]) == 7 for p in range(P)) and int(sig[:, 4:8].sum()) == 7 * P
+    assert int(counter[0]) == 0 and int(st[0]) == 0
+    assert torch.equal(qd[2][rank * Ls:(rank + 1) * Ls], q[:, 2 * Hp:3 * Hp])
+    # a wait on entries 4..7 of rank 0's array: only entry 5 (rank 1) holds an epoch
+    sig[0, 4:8] = 7
+    w_ok = RwSpSync(c_vp(sig_ptrs.data_ptr()), None, P, 0, 4, 7, 0, 0, 1000, 0)
+    assert lib.rw_sp_wait(ctypes.byref(w_ok), c_vp(st.data_ptr()), _native.stream_ptr(cuda)) == 0
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0
+    w_late = RwSpSync(c_vp(sig_ptrs.data_ptr()), None, P, 2, 4, 8, 0, 0, 100, 0)   # nobody signals epoch 8
+    assert lib.rw_sp_wait(ctypes.byref(w_late), c_vp(st.data_ptr()), _native.stream_ptr(cuda)) == 0
+    torch.cuda.synchronize()
+    assert int(st[0]) & 0x20
+    assert lib.rw_sp_wait(None, None, _native.stream_ptr(cuda)) == -1
+    x = torch.ones(16, device=cuda)
+    assert float((x * 2).sum()) == 32.0
+
+
 @pytest.mark.parametrize("P,rank", [(1, 0), (2, 1), (4, 2)])
 def test_sp_scatter_qkv_emulated_ranks(cuda, P, rank):
     """rw_sp_scatter_qkv of rank `rank` of P on one GPU: the P owners' buffers are
@@ -269,7 +315,7 @@ def test_sp_scatter_qkv_emulated_ranks(cuda, P, rank):
     code = _native.lib().rw_sp_scatter_qkv(
         c_vp(qg.data_ptr()), c_vp(kg.data_ptr()), c_vp(vg.data_ptr()), qg.stride(0), qg.stride(1),
         kg.stride(0), kg.stride(1), vg.stride(0), vg.stride(1), *(c_vp(t.data_ptr()) for t in ptrs),
-        Ls, H, 128, P, rank, d0, cap, ctypes.byref(rs), _native.stream_ptr(cuda))
+        Ls, H, 128, P, rank, d0, cap, ctypes.byref(rs), None, None, _native.stream_ptr(cuda))
     _native.check(code, "rw_sp_scatter_qkv")
     torch.cuda.synchronize()
     # the oracle's roped k for this rank's tokens (chunk positions rank * Ls + s)

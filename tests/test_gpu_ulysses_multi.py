@@ -134,3 +134,62 @@ def test_ulysses_p2p_two_gpus_match_single_gpu(tmp_path):
     Hp = H // 2
     for r in range(2):
         np.testing.assert_array_equal(np.load(tmp_path / f"p2p_k_r{r}.npy"), kr[:, :, r * Hp:(r + 1) * Hp])
+
+
+def _single_rank_worker(rank, world, port, out_dir):
+    """A group of one: the scatter signals its own rank, the attention waits for it
+    and signals again; five layer() calls alternate the q / output copies, with and
+    without the output wait."""
+    import sys
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, device_table, _native
+    from reworld_b200.ulysses import UlyssesP2P
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120), device_id=dev)
+    q, k, v, ck, cv = _inputs()
+    sp = UlyssesP2P(dist.group.WORLD, 2, (N_CACHED + 1) * L, L, H, device=dev)
+    n0 = N_CACHED * L
+    for layer in range(2):
+        sp.cache_k(layer)[:, :n0].copy_(ck[:, :n0].to(dev))
+        sp.cache_v(layer)[:, :n0].copy_(cv[:, :n0].to(dev))
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    outs = []
+    for call in range(5):
+        out = sp.layer(call % 2, q.to(dev), k.to(dev), v.to(dev), n0, rope=rope, sync_output=call % 2 == 0)
+        if call % 2 == 1:
+            sp.finish()
+        outs.append(out.float().cpu().numpy())
+    torch.cuda.synchronize()
+    _native.check_status(dev)
+    np.save(os.path.join(out_dir, "single.npy"), np.stack(outs))
+    np.save(os.path.join(out_dir, "single_counters.npy"), sp.counters.cpu().numpy())
+    dist.barrier()
+    del sp
+    dist.destroy_process_group()
+
+
+def test_ulysses_p2p_group_of_one_matches_chunk_attention(cuda, tmp_path):
+    """UlyssesP2P with one rank on one GPU (the scatter's signal and the attention's
+    wait and signal all on this rank, in stream order): every call equals the
+    single-GPU attention, and the completion counters end at zero."""
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table, rope_kv_store
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_single_rank_worker, args=(1, port, str(tmp_path)), nprocs=1, join=True)
+    q, k, v, ck, cv = _inputs()
+    ck, cv = ck.to(cuda), cv.to(cuda)
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), cuda), (F, HT, WT), N_CACHED * F)
+    n0 = N_CACHED * L
+    rope_kv_store(k.to(cuda), v.to(cuda), ck, cv, n0, rope=rope)
+    ref = chunk_attention(q.to(cuda), ck, cv, rope=rope).float().cpu().numpy()
+    got = np.load(tmp_path / "single.npy")
+    for g in got:
+        err = np.abs(g - ref)
+        assert err.max() < 2e-2 and err.mean() < 2e-3, (err.max(), err.mean())
+    assert not np.load(tmp_path / "single_counters.npy").any()
