@@ -203,7 +203,10 @@ extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, lo
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = Ls < sms * 16 ? Ls : sms * 16;
+    // with a signal every CTA ends with a system-scope fence: a few CTAs per SM, each
+    // walking several tokens, keep that cost small; without one, a CTA per token
+    const int cap_ctas = p.sync_on && p.sync.signal_epoch > 0 ? sms * 2 : sms * 16;
+    const int grid = Ls < cap_ctas ? Ls : cap_ctas;
     sp::scatter_qkv_kernel<<<grid, sp::SCATTER_THREADS, 0, (cudaStream_t)stream>>>(p);
   }
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
