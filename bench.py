@@ -794,7 +794,7 @@ def dropin_layer_measure(ro, dev, n_calls=6):
     (index bookkeeping, launches, host work) included.  Per call, against the
     attention kernel alone on the same shape."""
     import torch.nn as nn
-    from reworld_b200.self_attn import install
+    from reworld_b200.self_attn import install, write_index
     from reworld_b200.poses import random_walk
     C = HEADS * HEAD_DIM
 
@@ -831,34 +831,42 @@ def dropin_layer_measure(ro, dev, n_calls=6):
     y_host = torch.empty(1, CT, C, dtype=torch.bfloat16).pin_memory()
     seq_lens, grid = torch.tensor([CT]), torch.tensor([[FRAMES, TOK_H, TOK_W]])
 
-    def call():
-        cache["global_end_index"].fill_(n0)      # the same chunk position every call
-        cache["local_end_index"].fill_(n0)
-        x = x_host.to(dev, non_blocking=True)
-        y = mod.forward(x, seq_lens, grid, freqs, None, kv_cache=cache, current_start=n0, prope_context=ctx)
-        y_host.copy_(y, non_blocking=True)
+    x_dev = x_host.to(dev)
 
+    def call(host_io):
+        # the same chunk position every call (written the way the forward writes the
+        # indices, so their host mirrors stay valid and no call reads them back)
+        write_index(cache["global_end_index"], n0)
+        write_index(cache["local_end_index"], n0)
+        x = x_host.to(dev, non_blocking=True) if host_io else x_dev
+        y = mod.forward(x, seq_lens, grid, freqs, None, kv_cache=cache, current_start=n0, prope_context=ctx)
+        if host_io:
+            y_host.copy_(y, non_blocking=True)
+
+    res = {}
     with torch.no_grad():
-        for _ in range(2):
-            call()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n_calls):
-            call()
-        e1.record()
-        torch.cuda.synchronize()
-        wall = (time.perf_counter() - t0) / n_calls
-    ms = e0.elapsed_time(e1) / n_calls
+        for host_io in (False, True):
+            for _ in range(2):
+                call(host_io)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n_calls):
+                call(host_io)
+            e1.record()
+            torch.cuda.synchronize()
+            res[host_io] = (e0.elapsed_time(e1) / n_calls, (time.perf_counter() - t0) / n_calls)
+    ms, wall = res[False]
+    ms_io, _ = res[True]
     fl_attn = attn_flops(CT, LK, HEADS)
     fl_proj = 2.0 * CT * C * (3 * C + C + 2 * C)           # q|k|v, value_proj, o|prope_proj
     return {"ms_per_layer": round(ms, 4), "host_wall_ms_per_layer": round(wall * 1e3, 4),
             "tflops": round((fl_attn + fl_proj) / (ms * 1e-3) / 1e12, 1),
-            "h2d_bytes": CT * C * 2, "d2h_bytes": CT * C * 2,
+            "e2e_ms_per_layer": round(ms_io, 4), "h2d_bytes": CT * C * 2, "d2h_bytes": CT * C * 2,
             "path": "installed prop_self_attn_forward (stacked q|k|v GEMM, fused RMSNorm/RoPE/cache store, PRoPE "
-                    "SE3 + value_proj GEMM with residual, attention, [y | P y] GEMM) with x from pinned host memory "
-                    "and the output to pinned host memory",
+                    "SE3 + value_proj GEMM with residual, attention, [y | P y] GEMM) as the model calls it, x on the "
+                    "device; e2e_ms_per_layer: x from pinned host memory and the output back to it on the same stream",
             "shape": f"x [1, {CT}, {C}], cache {LK} keys x {HEADS} heads, PRoPE context on"}
 
 
