@@ -57,32 +57,9 @@ struct Params {
   int* status;
 };
 
-// floor(n / d) from m = floor((2^64 - 1) / d) + 1 (d >= 2): n * m / 2^64 exceeds
-// n / d by less than n / 2^64 < 1 / d, so the floor is exact for every 32-bit n.
-// m == 0 stands for d == 1.
-__device__ __forceinline__ uint32_t div_magic(uint32_t n, unsigned long long m) {
-  return m == 0 ? n : (uint32_t)__umul64hi((unsigned long long)n, m);
-}
-
 // rope_token with the two divisions by multiply-high.
 __device__ __forceinline__ RopeToken rope_token_magic(const Params& p, int token, int b) {
-  const rw_rope_t& rp = p.rope;
-  RopeToken rt;
-  const int hw = rp.grid_h * rp.grid_w;
-  rt.on = token < rp.grid_f * hw;
-  const uint32_t tok = rt.on ? (uint32_t)token : 0u;
-  const uint32_t f = div_magic(tok, p.m_hw);
-  const uint32_t rem = tok - f * (uint32_t)hw;
-  const uint32_t hh = div_magic(rem, p.m_w);
-  const uint32_t ww = rem - hh * (uint32_t)rp.grid_w;
-  const double2* tab = reinterpret_cast<const double2*>(rp.freqs);
-  rt.ft = tab + (size_t)(rp.start_frame + f) * 64;
-  rt.fh = tab + (size_t)hh * 64;
-  rt.fw = tab + (size_t)ww * 64;
-  rt.dl = rp.delta_cs ? reinterpret_cast<const float2*>(rp.delta_cs) + ((size_t)b * rp.grid_f + f) * 64 : nullptr;
-  rt.e_t = rp.c_t;
-  rt.e_h = rp.c_t + rp.c_h;
-  return rt;
+  return rope_token_fast(p.rope, (uint32_t)token, (uint32_t)b, p.m_hw, p.m_w);
 }
 
 // A packed bf16 pair widened to an fp32 pair (exact).
@@ -348,9 +325,8 @@ extern "C" int rw_qkv_norm_rope_store(const void* q_in, const void* k_in, const 
     p.rope_on = 1;
   }
   if (rope != nullptr) {
-    const unsigned long long hw = (unsigned long long)rope->grid_h * rope->grid_w;
-    p.m_hw = hw >= 2 ? ~0ull / hw + 1 : 0;
-    p.m_w = rope->grid_w >= 2 ? ~0ull / (unsigned long long)rope->grid_w + 1 : 0;
+    p.m_hw = div_magic_of((unsigned long long)rope->grid_h * rope->grid_w);
+    p.m_w = div_magic_of((unsigned long long)rope->grid_w);
   }
   const int stage_bytes = 6 * C;
   int slots = qkvn::STAGE_BUDGET / stage_bytes;  // one stage per token slot (warp pair)

@@ -43,6 +43,36 @@ __device__ __forceinline__ RopeToken rope_token(const rw_rope_t& rp, int token, 
   return rt;
 }
 
+// floor(n / d) from m = floor((2^64 - 1) / d) + 1 (d >= 2): n * m / 2^64 exceeds
+// n / d by less than n / 2^64 < 1 / d, so the floor is exact for every 32-bit n.
+// m == 0 stands for d == 1.
+__device__ __forceinline__ uint32_t div_magic(uint32_t n, unsigned long long m) {
+  return m == 0 ? n : (uint32_t)__umul64hi((unsigned long long)n, m);
+}
+inline unsigned long long div_magic_of(unsigned long long d) { return d >= 2 ? ~0ull / d + 1 : 0; }
+
+// rope_token with the two divisions by multiply-high: m_hw = div_magic_of(grid_h *
+// grid_w), m_w = div_magic_of(grid_w).
+__device__ __forceinline__ RopeToken rope_token_fast(const rw_rope_t& rp, uint32_t token, uint32_t b,
+                                                     unsigned long long m_hw, unsigned long long m_w) {
+  RopeToken rt;
+  const uint32_t hw = (uint32_t)(rp.grid_h * rp.grid_w);
+  rt.on = token < (uint32_t)rp.grid_f * hw;
+  const uint32_t tok = rt.on ? token : 0u;
+  const uint32_t f = div_magic(tok, m_hw);
+  const uint32_t rem = tok - f * hw;
+  const uint32_t hh = div_magic(rem, m_w);
+  const uint32_t ww = rem - hh * (uint32_t)rp.grid_w;
+  const double2* tab = reinterpret_cast<const double2*>(rp.freqs);
+  rt.ft = tab + (size_t)(rp.start_frame + f) * 64;
+  rt.fh = tab + (size_t)hh * 64;
+  rt.fw = tab + (size_t)ww * 64;
+  rt.dl = rp.delta_cs ? reinterpret_cast<const float2*>(rp.delta_cs) + ((size_t)b * rp.grid_f + f) * 64 : nullptr;
+  rt.e_t = rp.c_t;
+  rt.e_h = rp.c_t + rp.c_h;
+  return rt;
+}
+
 // The freqs entry of complex pair j of the token.
 __device__ __forceinline__ double2 rope_freq(int j, const RopeToken& rt) {
   return (j < rt.e_t) ? rt.ft[j] : ((j < rt.e_h) ? rt.fh[j] : rt.fw[j]);

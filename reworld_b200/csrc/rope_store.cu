@@ -21,10 +21,12 @@ struct Params {
   uint8_t* ck;
   uint8_t* cv;
   int B, L, H, dst_start;
+  // strides in bytes
   long long k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, q_sb, q_sl, q_sh, qo_sb, qo_sl, qo_sh;
   long long ck_sb, ck_sl, ck_sh, cv_sb, cv_sl, cv_sh;
   int rope_on;
   rw_rope_t rope;
+  unsigned long long m_L, m_hw, m_w;  // division magics of L, grid_h * grid_w and grid_w
 };
 
 __device__ __forceinline__ uint4 ldg16(const uint8_t* p) {
@@ -32,7 +34,9 @@ __device__ __forceinline__ uint4 ldg16(const uint8_t* p) {
 }
 __device__ __forceinline__ void stg16(uint8_t* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
-constexpr int THREADS = 128;  // a multiple of 16: a thread's chunks all sit at one place in their head
+constexpr int THREADS = 128;         // a multiple of 16: a thread's chunks all sit at one place in their head
+constexpr int HSTEP = THREADS / 16;  // heads between two chunks of a thread
+constexpr int NB = 3;                // chunks per thread and batch (24 heads: one batch)
 
 // The 4 RoPE pairs of chunk position c16 of the token (same for every head).
 struct RopeRegs {
@@ -41,8 +45,8 @@ struct RopeRegs {
   bool rot, has_d;
 };
 
-__device__ __forceinline__ void rope_regs(const rw_rope_t& rp, int t, int b, int c16, RopeRegs& r) {
-  const RopeToken rt = rope_token(rp, t, b);
+__device__ __forceinline__ void rope_regs(const Params& p, uint32_t t, uint32_t b, int c16, RopeRegs& r) {
+  const RopeToken rt = rope_token_fast(p.rope, t, b, p.m_hw, p.m_w);
   r.rot = rt.on;
   r.has_d = rt.dl != nullptr;
 #pragma unroll
@@ -60,36 +64,51 @@ __device__ __forceinline__ uint4 rotate(uint4 v, const RopeRegs& r) {
   return v;
 }
 
-// CTAs walk the tokens (b, t); a thread handles the token's chunks threadIdx.x,
-// threadIdx.x + 128, ... (all at chunk position c16 = threadIdx.x mod 16 of
-// their head), so the token's position and this thread's 4 RoPE table entries
-// are looked up once per token.
-__global__ void __launch_bounds__(THREADS) rope_kv_store_kernel(const __grid_constant__ Params p) {
-  const long long tokens = (long long)p.B * p.L;
-  const int nch = p.H * 16;
+// CTAs walk the tokens (b, t); thread x handles the 16-byte chunk c16 = x mod 16
+// of heads x / 16, x / 16 + 8, ..., so the token's position and the thread's 4
+// RoPE table entries are looked up once per token, and its row addresses once per
+// token (then one add per head).  The loads of a batch of NB heads are all issued
+// before the batch's first store, so one round trip to memory covers them.
+__global__ void __launch_bounds__(THREADS, 4) rope_kv_store_kernel(const __grid_constant__ Params p) {
+  const uint32_t tokens = (uint32_t)p.B * (uint32_t)p.L;  // < 2^31 (host check)
   const int c16 = threadIdx.x & 15;
-  const long long eoff = (long long)c16 * 8;  // element offset within the head row
-  for (long long tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
-    const int b = (int)(tok / p.L);
-    const int t = (int)(tok - (long long)b * p.L);
-    RopeRegs r;
-    r.rot = false;
-    if (p.rope_on) rope_regs(p.rope, t, b, c16, r);
-    const long long td = (long long)p.dst_start + t;
-    for (int c = threadIdx.x; c < nch; c += THREADS) {
-      const long long h = c >> 4;
-      // V: plain copy into the cache slot
-      const uint4 vv = ldg16(p.v + 2 * (b * p.v_sb + t * p.v_sl + h * p.v_sh + eoff));
-      stg16(p.cv + 2 * (b * p.cv_sb + td * p.cv_sl + h * p.cv_sh + eoff), vv);
-      // K: rotate, then store into the cache slot
-      uint4 kv = ldg16(p.k + 2 * (b * p.k_sb + t * p.k_sl + h * p.k_sh + eoff));
-      if (r.rot) kv = rotate(kv, r);
-      stg16(p.ck + 2 * (b * p.ck_sb + td * p.ck_sl + h * p.ck_sh + eoff), kv);
-      // Q: optional rotated copy
-      if (p.q_in != nullptr) {
-        uint4 qv = ldg16(p.q_in + 2 * (b * p.q_sb + t * p.q_sl + h * p.q_sh + eoff));
-        if (r.rot) qv = rotate(qv, r);
-        stg16(p.q_out + 2 * (b * p.qo_sb + t * p.qo_sl + h * p.qo_sh + eoff), qv);
+  const int h0 = threadIdx.x >> 4;
+  const long long e = 16LL * c16;  // byte offset of the chunk within the head row
+  const bool with_q = p.q_in != nullptr;
+  for (uint32_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+    const uint32_t b = div_magic(tok, p.m_L);
+    const uint32_t t = tok - b * (uint32_t)p.L;
+    const uint32_t td = (uint32_t)p.dst_start + t;
+    const uint8_t* kp = p.k + b * p.k_sb + t * p.k_sl + e;
+    const uint8_t* vp = p.v + b * p.v_sb + t * p.v_sl + e;
+    uint8_t* ckp = p.ck + b * p.ck_sb + td * p.ck_sl + e;
+    uint8_t* cvp = p.cv + b * p.cv_sb + td * p.cv_sl + e;
+    const uint8_t* qp = with_q ? p.q_in + b * p.q_sb + t * p.q_sl + e : nullptr;
+    uint8_t* qop = with_q ? p.q_out + b * p.qo_sb + t * p.qo_sl + e : nullptr;
+    for (int hb = h0; hb < p.H; hb += HSTEP * NB) {
+      uint4 kv[NB], vv[NB], qv[NB];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const long long h = hb + j * HSTEP;
+        if (h < p.H) {
+          vv[j] = ldg16(vp + h * p.v_sh);
+          kv[j] = ldg16(kp + h * p.k_sh);
+          if (with_q) qv[j] = ldg16(qp + h * p.q_sh);
+        }
+      }
+      RopeRegs r;
+      r.rot = false;
+      if (p.rope_on) rope_regs(p, t, b, c16, r);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const long long h = hb + j * HSTEP;
+        if (h < p.H) {
+          // V: plain copy into the cache slot; K: rotated into the cache slot
+          stg16(cvp + h * p.cv_sh, vv[j]);
+          stg16(ckp + h * p.ck_sh, r.rot ? rotate(kv[j], r) : kv[j]);
+          // Q: optional rotated copy
+          if (with_q) stg16(qop + h * p.qo_sh, r.rot ? rotate(qv[j], r) : qv[j]);
+        }
       }
     }
   }
@@ -122,6 +141,7 @@ extern "C" int rw_rope_kv_store(const void* k, const void* v, const void* q_in, 
     if ((i % 3) == 0 && B == 1) continue;
     if (st[i] < 0 || (st[i] % 8) != 0) return RW_ERR_INVALID_ARG;
   }
+  if ((long long)B * L >= (1LL << 31)) return RW_ERR_UNSUPPORTED;
   store::Params p{};
   p.k = (const uint8_t*)k;
   p.v = (const uint8_t*)v;
@@ -132,24 +152,29 @@ extern "C" int rw_rope_kv_store(const void* k, const void* v, const void* q_in, 
   p.L = L;
   p.H = H;
   p.dst_start = dst_start;
-  p.k_sb = B == 1 ? 0 : k_sb; p.k_sl = k_sl; p.k_sh = k_sh;
-  p.v_sb = B == 1 ? 0 : v_sb; p.v_sl = v_sl; p.v_sh = v_sh;
-  p.q_sb = B == 1 ? 0 : q_sb; p.q_sl = q_sl; p.q_sh = q_sh;
-  p.qo_sb = B == 1 ? 0 : qo_sb; p.qo_sl = qo_sl; p.qo_sh = qo_sh;
-  p.ck_sb = B == 1 ? 0 : ck_sb; p.ck_sl = ck_sl; p.ck_sh = ck_sh;
-  p.cv_sb = B == 1 ? 0 : cv_sb; p.cv_sl = cv_sl; p.cv_sh = cv_sh;
+  // element strides -> byte strides (batch strides unused when B == 1)
+  const auto bs = [B](long long s) { return B == 1 ? 0LL : 2 * s; };
+  p.k_sb = bs(k_sb); p.k_sl = 2 * k_sl; p.k_sh = 2 * k_sh;
+  p.v_sb = bs(v_sb); p.v_sl = 2 * v_sl; p.v_sh = 2 * v_sh;
+  p.q_sb = bs(q_sb); p.q_sl = 2 * q_sl; p.q_sh = 2 * q_sh;
+  p.qo_sb = bs(qo_sb); p.qo_sl = 2 * qo_sl; p.qo_sh = 2 * qo_sh;
+  p.ck_sb = bs(ck_sb); p.ck_sl = 2 * ck_sl; p.ck_sh = 2 * ck_sh;
+  p.cv_sb = bs(cv_sb); p.cv_sl = 2 * cv_sl; p.cv_sh = 2 * cv_sh;
   p.rope_on = 0;
   if (rope != nullptr) {
     if (!rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
     p.rope = *rope;
     p.rope_on = 1;
+    p.m_hw = div_magic_of((unsigned long long)rope->grid_h * rope->grid_w);
+    p.m_w = div_magic_of((unsigned long long)rope->grid_w);
   }
   p.B = B;
+  p.m_L = div_magic_of((unsigned long long)L);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long tokens = (long long)B * L;
-  const long long cap = (long long)sms * 16;  // 16 resident 128-thread CTAs per SM, tokens strided over them
+  const long long cap = (long long)sms * 16;  // resident 128-thread CTAs, tokens strided over them
   const long long grid = tokens < cap ? tokens : cap;
   store::rope_kv_store_kernel<<<(unsigned)grid, store::THREADS, 0, (cudaStream_t)stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
