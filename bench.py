@@ -865,7 +865,8 @@ def dropin_layer_measure(ro, dev, n_calls=6):
             "tflops": round((fl_attn + fl_proj) / (ms * 1e-3) / 1e12, 1),
             "e2e_ms_per_layer": round(ms_io, 4), "h2d_bytes": CT * C * 2, "d2h_bytes": CT * C * 2,
             "path": "installed prop_self_attn_forward (stacked q|k|v GEMM, fused RMSNorm/RoPE/cache store, PRoPE "
-                    "SE3 + value_proj GEMM with residual, attention, [y | P y] GEMM) as the model calls it, x on the "
+                    "SE3 + value_proj GEMM with residual, attention writing y and P y, [y | P y] GEMM) as the model "
+                    "calls it, x on the "
                     "device; e2e_ms_per_layer: x from pinned host memory and the output back to it on the same stream",
             "shape": f"x [1, {CT}, {C}], cache {LK} keys x {HEADS} heads, PRoPE context on"}
 

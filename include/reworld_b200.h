@@ -77,6 +77,23 @@ int rw_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int
                 float softmax_scale, const rw_rope_t* rope, void* workspace, long long workspace_bytes,
                 int* status, void* stream);
 
+/* rw_attn_fwd that also writes P y, the PRoPE O-side transform of its output,
+ * for the cached self-attention's [y | P y] output projection: po[b, t, h, 4g + i]
+ * = sum_k mats[b, t / frame_seqlen][i][k] * y[b, t, h, 4g + k] from the bf16
+ * output values y, bit for bit what rw_se3_block_apply(y, po, mats, ...) writes,
+ * without reading y back (the attention's epilogue and merge write both).
+ * Replaces action_model.py:302 followed by _se3_block_apply(x, ..., "P") at
+ * :307-312 (wan_5b/modules/action_model.py:84-114).  mats: [B, Lq /
+ * frame_seqlen, 4, 4] fp32 (16-byte aligned); po: [B, Lq, H, 128] bf16 with
+ * strides po_*; Lq a multiple of frame_seqlen.  Other arguments as rw_attn_fwd. */
+int rw_attn_fwd_prope(const void* q, const void* k, const void* v, void* o, void* po, const float* mats,
+                      int frame_seqlen, int B, int Lq, int Lk, int H, int D, long long q_sb, long long q_sl,
+                      long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
+                      long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh,
+                      long long po_sb, long long po_sl, long long po_sh, float softmax_scale,
+                      const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status,
+                      void* stream);
+
 /* Workspace bytes rw_attn_fwd uses for this shape on the current device (0 when
  * the work fills whole waves). */
 long long rw_attn_workspace_bytes(int B, int Lq, int Lk, int H);

@@ -56,6 +56,8 @@ class RwCopyDesc(ctypes.Structure):
 _SIGNATURES = {
     "rw_attn_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int] + [c_ll] * 12
                     + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
+    "rw_attn_fwd_prope": (c_int, [c_vp] * 6 + [c_int] * 6 + [c_ll] * 15
+                          + [c_float, ctypes.POINTER(RwRope), c_vp, c_ll, c_vp, c_vp]),
     "rw_attn_workspace_bytes": (c_ll, [c_int, c_int, c_int, c_int]),
     "rw_attn_fwd_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int] + [c_ll] * 12
                             + [c_float, ctypes.POINTER(RwRope), c_vp, c_vp]),
@@ -82,7 +84,7 @@ _SIGNATURES = {
     "rw_abi_version": (c_int, []),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 _lib = None
 
 

@@ -41,12 +41,17 @@ def _workspace(device, nbytes):
     return ws
 
 
-def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None):
+def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None, se3=None):
     """softmax(q k^T * scale) v over every key (no mask), bf16, fp32 accumulation.
 
     q: [B, Lq, H, 128]; k, v: [B, Lk, H, 128] (any strides with a contiguous head
     dim, e.g. kv_cache["k"][:, :local_end]).  `rope` (a RopeArgs) applies the
     3-D RoPE (+ PM-RoPE phase) to q inside the kernel.  Returns bf16 [B, Lq, H, 128].
+
+    se3 = (mats, frame_seqlen, po): the kernel also writes po = P y, the PRoPE
+    O-side transform of its output (mats: fp32 [B, Lq / frame_seqlen, 4, 4]; po:
+    bf16 [B, Lq, H, 128], e.g. the right half of the [y | P y] rows), as
+    rw_se3_block_apply would from y (rw_attn_fwd_prope).
     """
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise ValueError("chunk_attention runs on CUDA tensors only")
@@ -64,20 +69,34 @@ def chunk_attention(q, k, v, softmax_scale=None, rope=None, out=None):
     scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(D)
     rope_struct = rope.struct() if rope is not None else None
     lib = _native.lib()
+    if se3 is not None:
+        mats, fs, po = se3
+        if mats.dtype != torch.float32 or not mats.is_contiguous() or mats.device != q.device or \
+                mats.shape != (B, Lq // int(fs), 4, 4) or Lq % int(fs) != 0:
+            raise ValueError("se3 matrices must be fp32 [B, Lq / frame_seqlen, 4, 4] on q's device")
+        if po.dtype != torch.bfloat16 or po.shape != (B, Lq, H, D) or not _strides_ok(po):
+            raise ValueError("se3 output must be a bf16 [B, Lq, H, D] tensor with a contiguous head dim")
     with torch.cuda.device(q.device):
         st = _native.status_tensor(q.device)
         ws = _workspace(q.device, lib.rw_attn_workspace_bytes(B, Lq, Lk, H))
-        code = lib.rw_attn_fwd(
-            c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()), c_vp(out.data_ptr()),
-            B, Lq, Lk, H, D,
-            q.stride(0), q.stride(1), q.stride(2),
-            k.stride(0), k.stride(1), k.stride(2),
-            v.stride(0), v.stride(1), v.stride(2),
-            out.stride(0), out.stride(1), out.stride(2),
-            scale, ctypes.byref(rope_struct) if rope_struct is not None else None,
-            c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
-            c_vp(st.data_ptr()), _native.stream_ptr(q.device))
-    _native.check(code, "rw_attn_fwd")
+        common = (B, Lq, Lk, H, D,
+                  q.stride(0), q.stride(1), q.stride(2),
+                  k.stride(0), k.stride(1), k.stride(2),
+                  v.stride(0), v.stride(1), v.stride(2),
+                  out.stride(0), out.stride(1), out.stride(2))
+        tail = (scale, ctypes.byref(rope_struct) if rope_struct is not None else None,
+                c_vp(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+                c_vp(st.data_ptr()), _native.stream_ptr(q.device))
+        if se3 is None:
+            name = "rw_attn_fwd"
+            code = lib.rw_attn_fwd(c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()),
+                                   c_vp(out.data_ptr()), *common, *tail)
+        else:
+            name = "rw_attn_fwd_prope"
+            code = lib.rw_attn_fwd_prope(c_vp(q.data_ptr()), c_vp(k.data_ptr()), c_vp(v.data_ptr()),
+                                         c_vp(out.data_ptr()), c_vp(po.data_ptr()), c_vp(mats.data_ptr()), int(fs),
+                                         *common, po.stride(0), po.stride(1), po.stride(2), *tail)
+    _native.check(code, name)
     return out
 
 

@@ -13,4 +13,4 @@ extern "C" const char* rw_error_string(int code) {
   }
 }
 
-extern "C" int rw_abi_version(void) { return 3; }
+extern "C" int rw_abi_version(void) { return 4; }

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
+#include "se3.cuh"
 #include "sp_sync.cuh"
 
 namespace rw {
@@ -54,7 +55,7 @@ __device__ __forceinline__ void combine_unit(const float* __restrict__ scratch, 
                                              long long o_sb, long long o_sl, long long o_sh, int Lq, int H, int nqp,
                                              int n_kv, int U, int Np, float scale_log2,
                                              const unsigned long long* __restrict__ peer_ptrs, int peer_Ls,
-                                             int peer_H, int peer_h0) {
+                                             int peer_H, int peer_h0, const Se3Out& se3) {
   const int base = (U / Np) * Np;                  // units of the waves (written whole)
   const int unit = base + (int)blockIdx.x, i = blockIdx.y, c0 = blockIdx.z * COMBINE_COLS, r = threadIdx.x;
   const long long T = (long long)(U - base) * n_kv;
@@ -95,6 +96,15 @@ __device__ __forceinline__ void combine_unit(const float* __restrict__ scratch, 
     row_base = out + 2 * ((long long)bb * o_sb + (long long)row_tok * o_sl + head * o_sh);
   }
   uint4* dst = reinterpret_cast<uint4*>(row_base + 2 * c0);
+  // optional P y beside y (local output only): the row's frame matrix times the
+  // bf16 output values
+  float pm[16];
+  uint4* pdst = nullptr;
+  if (se3.mats != nullptr && peer_ptrs == nullptr) {
+    se3_mat(se3.mats, se3.frames, bb, row_tok / se3.fs, pm);
+    pdst = reinterpret_cast<uint4*>(
+        se3.out + 2 * ((long long)bb * se3.sb + (long long)row_tok * se3.sl + head * se3.sh + c0));
+  }
 #pragma unroll
   for (int q = 0; q < COMBINE_COLS / 8; ++q) {
     uint4 v;
@@ -103,6 +113,7 @@ __device__ __forceinline__ void combine_unit(const float* __restrict__ scratch, 
     v.z = pack_bf16x2(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
     v.w = pack_bf16x2(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
     dst[q] = v;
+    if (pdst != nullptr) pdst[q] = se3_chunk(pm, v);
   }
 }
 
@@ -110,9 +121,9 @@ __global__ void __launch_bounds__(128)
     combine_kernel(const float* __restrict__ scratch, uint8_t* __restrict__ out, long long o_sb, long long o_sl,
                    long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
                    const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0,
-                   const __grid_constant__ rw_sp_sync_t sync, int sync_signal) {
+                   const __grid_constant__ rw_sp_sync_t sync, int sync_signal, const __grid_constant__ Se3Out se3) {
   combine_unit(scratch, out, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, U, Np, scale_log2, peer_ptrs, peer_Ls, peer_H,
-               peer_h0);
+               peer_h0, se3);
   if (sync_signal) sp_signal_done(sync);  // every merged row is at its owner rank
 }
 
@@ -146,7 +157,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
            const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, const rw_sp_sync_t* sync,
-           bool sync_signal, cudaStream_t stream);
+           bool sync_signal, const Se3Out& se3, cudaStream_t stream);
 }  // namespace pair
 }  // namespace rw
 
@@ -171,7 +182,7 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
              long long q_sl, long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
              long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float softmax_scale,
              const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status, void* stream,
-             const PeerArgs& peer) {
+             const PeerArgs& peer, const Se3Out& se3) {
   if (!q || !k || !v || !o) return RW_ERR_INVALID_ARG;
   if (D != attn::HD) return RW_ERR_UNSUPPORTED;
   if (B < 1 || Lq < 1 || Lk < 1 || H < 1 || B > 65535 || H > 65535) return RW_ERR_INVALID_ARG;
@@ -184,6 +195,15 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
     if (!stride_ok(strides[i])) return RW_ERR_INVALID_ARG;
   }
   if (rope != nullptr && !rope_args_ok(*rope, D)) return RW_ERR_INVALID_ARG;
+  if (se3.mats != nullptr) {
+    // P y beside y: local output only, whole frames, 16-byte aligned rows
+    if (peer.ptrs != nullptr) return RW_ERR_UNSUPPORTED;
+    if (se3.out == nullptr || se3.fs < 1 || Lq % se3.fs != 0 || se3.frames != Lq / se3.fs) return RW_ERR_INVALID_ARG;
+    if (!aligned16(se3.mats) || !aligned16(se3.out)) return RW_ERR_INVALID_ARG;
+    const long long ps[3] = {se3.sb, se3.sl, se3.sh};
+    for (int i = 0; i < 3; ++i)
+      if (!(i == 0 && B == 1) && !stride_ok(ps[i])) return RW_ERR_INVALID_ARG;
+  }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   const int nqp = (Lq + 2 * attn::BM - 1) / (2 * attn::BM);
   const int n_kv = (Lk + attn::BN - 1) / attn::BN;
@@ -194,7 +214,7 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
   // with a sync record the signal comes from the last kernel that writes output rows
   const int rc = pair::launch(q, k, v, o, B, Lq, Lk, H, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb,
                               o_sl, o_sh, scale_log2, rope, status, wk.shared ? (float*)workspace : nullptr, nqp,
-                              units, wk.Np, peer.ptrs, peer.Ls, peer.H, peer.h0, peer.sync, !wk.shared,
+                              units, wk.Np, peer.ptrs, peer.Ls, peer.H, peer.h0, peer.sync, !wk.shared, se3,
                               (cudaStream_t)stream);
   if (rc != RW_OK) return rc;
   if (wk.shared) {
@@ -203,7 +223,7 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
     const bool sig = peer.sync != nullptr && peer.sync->signal_epoch > 0;
     attn::combine_kernel<<<dim3(tail_units, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
         (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, units, wk.Np, scale_log2,
-        peer.ptrs, peer.Ls, peer.H, peer.h0, sig ? *peer.sync : none, sig ? 1 : 0);
+        peer.ptrs, peer.Ls, peer.H, peer.h0, sig ? *peer.sync : none, sig ? 1 : 0, se3);
     if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
   }
   return RW_OK;
@@ -218,7 +238,21 @@ extern "C" int rw_attn_fwd(const void* q, const void* k, const void* v, void* o,
                            void* workspace, long long workspace_bytes, int* status, void* stream) {
   return attn_run(q, k, v, o, B, Lq, Lk, H, D, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb, o_sl,
                   o_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
-                  PeerArgs{nullptr, 0, 0, 0, nullptr});
+                  PeerArgs{nullptr, 0, 0, 0, nullptr}, Se3Out{});
+}
+
+extern "C" int rw_attn_fwd_prope(const void* q, const void* k, const void* v, void* o, void* po, const float* mats,
+                                 int frame_seqlen, int B, int Lq, int Lk, int H, int D, long long q_sb, long long q_sl,
+                                 long long q_sh, long long k_sb, long long k_sl, long long k_sh, long long v_sb,
+                                 long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh,
+                                 long long po_sb, long long po_sl, long long po_sh, float softmax_scale,
+                                 const rw_rope_t* rope, void* workspace, long long workspace_bytes, int* status,
+                                 void* stream) {
+  if (mats == nullptr || po == nullptr || frame_seqlen < 1) return RW_ERR_INVALID_ARG;
+  const Se3Out se3{mats, (uint8_t*)po, B == 1 ? 0 : po_sb, po_sl, po_sh, frame_seqlen, Lq / frame_seqlen};
+  return attn_run(q, k, v, o, B, Lq, Lk, H, D, q_sb, q_sl, q_sh, k_sb, k_sl, k_sh, v_sb, v_sl, v_sh, o_sb, o_sl,
+                  o_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
+                  PeerArgs{nullptr, 0, 0, 0, nullptr}, se3);
 }
 
 extern "C" int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int Lq, int Lk, int Hp, int D,
@@ -233,5 +267,5 @@ extern "C" int rw_sp_attn_fwd(const void* q, const void* k, const void* v, int L
   // o is never written in this mode; q's layout stands in for it in the unused output map
   return attn_run(q, k, v, const_cast<void*>(q), 1, Lq, Lk, Hp, D, 0, q_sl, q_sh, 0, k_sl, k_sh, 0, v_sl, v_sh, 0,
                   q_sl, q_sh, softmax_scale, rope, workspace, workspace_bytes, status, stream,
-                  PeerArgs{out_ptrs, Lq / P, H, rank * Hp, sync});
+                  PeerArgs{out_ptrs, Lq / P, H, rank * Hp, sync}, Se3Out{});
 }

@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "host_util.h"
 #include "rope.cuh"
+#include "se3.cuh"
 #include "sp_sync.cuh"
 
 namespace rw {
@@ -103,6 +104,7 @@ struct Params {
   int sync_wait;    // 1: every CTA's producer waits for the ranks' scatters before its first load
   int sync_signal;  // 1: the last CTA to finish signals the ranks (no merge kernel follows)
   rw_sp_sync_t sync;
+  Se3Out se3;       // se3.mats != nullptr: whole units also store P y through tm_po (local output only)
 };
 
 struct __align__(8) Barriers {
@@ -225,7 +227,7 @@ __device__ __forceinline__ void rope_row_half(uint8_t* tile, int r, int h, int t
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                     const __grid_constant__ Params p) {
+                     const __grid_constant__ CUtensorMap tm_po, const __grid_constant__ Params p) {
   extern __shared__ uint8_t dsmem_raw[];
   __shared__ Barriers sb;
   __shared__ float m_sh[NSBUF][BM];    // running maximum handed from key tile j to j + 1
@@ -650,6 +652,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // completed before o_done) -> TMA store; warpgroup w writes box w
       tc_fence_after();
       const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      // with P y: the row's frame matrix (rows past Lq, clipped by the store, use frame 0);
+      // P y is staged in the first K/V stage, idle once every PV completed (o_done)
+      // until the next segment's loads, which start after the boundary
+      const bool with_po = p.se3.mats != nullptr;
+      float m[16];
+      if (with_po) se3_mat(p.se3.mats, p.se3.frames, bidx, row0 + r < p.Lq ? (row0 + r) / p.se3.fs : 0, m);
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
@@ -664,7 +672,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           v.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
           v.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
           v.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
-          *reinterpret_cast<uint4*>(smem_q + w * Q_HALF + r * 128 + ((chunk ^ (r & 7)) << 4)) = v;
+          const int off = w * Q_HALF + r * 128 + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(smem_q + off) = v;
+          if (with_po) *reinterpret_cast<uint4*>(stages + off) = se3_chunk(m, v);
         }
       }
       fence_proxy_async_smem();
@@ -673,6 +683,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (pwait(&sb.epi, (uint32_t)n_epi & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)) {
           tma_store_4d(&tm_o, smem_q, 0, head, row0, bidx);
           tma_store_4d(&tm_o, smem_q + Q_HALF, 64, head, row0, bidx);
+          if (with_po) {
+            tma_store_4d(&tm_po, stages, 0, head, row0, bidx);
+            tma_store_4d(&tm_po, stages + Q_HALF, 64, head, row0, bidx);
+          }
           bulk_commit_group();
           bulk_wait_group_read<0>();
         }
@@ -750,12 +764,16 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
            long long v_sl, long long v_sh, long long o_sb, long long o_sl, long long o_sh, float scale_log2,
            const rw_rope_t* rope, int* status, float* scratch, int nqp, int U, int Np,
            const unsigned long long* peer_ptrs, int peer_Ls, int peer_H, int peer_h0, const rw_sp_sync_t* sync,
-           bool sync_signal, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv, mo;
+           bool sync_signal, const Se3Out& se3, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, mo, mpo;
   if (make_bf16_bl_hd_map(&mq, q, B, Lq, H, HD, q_sb, q_sl, q_sh, BM) ||
       make_bf16_bl_hd_map(&mk, k, B, Lk, H, HD, k_sb, k_sl, k_sh, BN / 2) ||
       make_bf16_bl_hd_map(&mv, v, B, Lk, H, HD, v_sb, v_sl, v_sh, BN) ||
       make_bf16_bl_hd_map(&mo, o, B, Lq, H, HD, o_sb, o_sl, o_sh, BM))
+    return RW_ERR_DRIVER;
+  if (se3.mats == nullptr)
+    mpo = mo;  // unused
+  else if (make_bf16_bl_hd_map(&mpo, se3.out, B, Lq, H, HD, se3.sb, se3.sl, se3.sh, BM))
     return RW_ERR_DRIVER;
   static std::atomic<unsigned long long> attr_done{0};
   if (!ensure_smem_attr((const void*)attn_pair_kernel, SMEM_BYTES, &attr_done)) return RW_ERR_CUDA;
@@ -771,6 +789,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   prm.status = status;
   prm.scratch = scratch;
   prm.peer = PeerOut{peer_ptrs, peer_Ls, peer_H, peer_h0};
+  prm.se3 = se3;
   prm.rope_on = 0;
   if (rope != nullptr) {
     prm.rope = *rope;
@@ -785,7 +804,7 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   }
   if (Np < 1 || U < 1 || 2LL * Np > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
   if (U % Np != 0 && (long long)(U % Np) * ((Lk + BN - 1) / BN) < Np) return RW_ERR_INVALID_ARG;  // empty tail shares
-  attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+  attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, mpo, prm);
   return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
 

@@ -6,10 +6,8 @@
 // the V-side P^-1 residual (:194-203) and the O-side P residual (:307-318).  The
 // matrices come from the host already in the activation dtype's values (the
 // reference casts the context to bf16 and, for P^-1, inverts it in bf16) and
-// are passed as fp32.  Each output is an fp32 sum of the 4 exact bf16 x bf16
-// products (fused multiply-adds in k order from +0) rounded once to bf16, as a
-// bf16 matmul with fp32 accumulation rounds it; only the order of the 4-term sum
-// can differ from the library's.
+// are passed as fp32; the arithmetic is se3.cuh's (only the order of the 4-term
+// sum can differ from the library's).
 //
 // CTAs of 64 threads walk the tokens (the token's frame matrix is loaded once);
 // a thread transforms 16-byte chunks (two groups of 4), their loads issued
@@ -17,6 +15,7 @@
 // and 2 bytes written per element.
 #include "common.cuh"
 #include "host_util.h"
+#include "se3.cuh"
 
 namespace rw {
 namespace se3 {
@@ -29,22 +28,6 @@ struct Params {
   int B, L, H, fs, frames;
 };
 
-__device__ __forceinline__ void apply_group(const float (&m)[16], uint32_t a, uint32_t b, uint32_t& ya,
-                                            uint32_t& yb) {
-  const float x[4] = {bf16_lo(a), bf16_hi(a), bf16_lo(b), bf16_hi(b)};
-  float y[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float acc = __fmaf_rn(m[4 * i], x[0], 0.f);  // from +0, like a BLAS accumulator
-    acc = __fmaf_rn(m[4 * i + 1], x[1], acc);
-    acc = __fmaf_rn(m[4 * i + 2], x[2], acc);
-    acc = __fmaf_rn(m[4 * i + 3], x[3], acc);
-    y[i] = acc;
-  }
-  ya = pack_bf16x2(y[0], y[1]);
-  yb = pack_bf16x2(y[2], y[3]);
-}
-
 constexpr int THREADS = 64;  // small CTAs, one per token; a thread's 6 chunks (24 heads) unrolled
 
 __global__ void __launch_bounds__(THREADS) se3_kernel(const __grid_constant__ Params p) {
@@ -54,26 +37,15 @@ __global__ void __launch_bounds__(THREADS) se3_kernel(const __grid_constant__ Pa
     const int b = (int)(tok / p.L);
     const int t = (int)(tok - (long long)b * p.L);
     const int f = t / p.fs;
-    const float4* mp = reinterpret_cast<const float4*>(p.mats + ((long long)b * p.frames + f) * 16);
     float m[16];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 r = __ldg(mp + j);
-      m[4 * j] = r.x;
-      m[4 * j + 1] = r.y;
-      m[4 * j + 2] = r.z;
-      m[4 * j + 3] = r.w;
-    }
+    se3_mat(p.mats, p.frames, b, f, m);
     const uint8_t* xr = p.x + 2 * ((long long)b * p.x_sb + (long long)t * p.x_sl);
     uint8_t* orow = p.out + 2 * ((long long)b * p.o_sb + (long long)t * p.o_sl);
 #pragma unroll 6
     for (int c = threadIdx.x; c < nch; c += THREADS) {
       const long long h = c >> 4, e = (long long)(c & 15) * 8;
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + 2 * (h * p.x_sh + e)));
-      uint4 o;
-      apply_group(m, v.x, v.y, o.x, o.y);
-      apply_group(m, v.z, v.w, o.z, o.w);
-      *reinterpret_cast<uint4*>(orow + 2 * (h * p.o_sh + e)) = o;
+      *reinterpret_cast<uint4*>(orow + 2 * (h * p.o_sh + e)) = se3_chunk(m, v);
     }
   }
 }

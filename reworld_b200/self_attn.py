@@ -318,13 +318,15 @@ def prop_self_attn_forward(self, x, seq_lens, grid_sizes, freqs, block_mask, kv_
         k_slice = kv_cache["k"][:, s0:local_end]
         v_slice = kv_cache["v"][:, s0:local_end]
     if fused and prope_context is not None:
-        # [y | P y] in one buffer: the attention writes y, the SE3 kernel P y, one GEMM does
-        # o(y) + prope_proj(P y) (action_model.py:307-318)
+        # [y | P y] in one buffer, both halves written by the attention (P y from its bf16
+        # output values, as _se3_block_apply forms it); one GEMM does o(y) + prope_proj(P y)
+        # (action_model.py:307-318)
         C = n * d
         yy = torch.empty((b, s, 2 * C), dtype=torch.bfloat16, device=x.device)
         y = yy[..., :C].view(b, s, n, d)
-        chunk_attention(q, k_slice, v_slice, rope=rope, out=y)
-        se3_block_apply(y, prope_context, "P", frame_seqlen, out=yy[..., C:].view(b, s, n, d), t_bound=t_bound)
+        mats = _cached_mats(prope_context, "P", s // frame_seqlen, torch.bfloat16, t_bound, x.device)
+        chunk_attention(q, k_slice, v_slice, rope=rope, out=y,
+                        se3=(mats, frame_seqlen, yy[..., C:].view(b, s, n, d)))
         write_index(kv_cache["global_end_index"], cur_end)
         write_index(kv_cache["local_end_index"], local_end)
         return gemm.linear(yy, *_stacked_out(self))

@@ -115,3 +115,54 @@ def test_se3_kernel_two_batches(cuda):
     torch.cuda.synchronize()
     u = _ulps(out.cpu(), want.contiguous())
     assert u.max() <= 1 and (u == 0).mean() > 0.99, (u.max(), (u == 0).mean())
+
+
+@pytest.mark.parametrize("B,Lq,Lk,H,fs,with_rope", [
+    (1, 2640, 7920, 24, 880, True),   # the 704x1280 chunk: whole units plus merged key-split tail units
+    (1, 512, 1024, 37, 128, False),   # 74 whole units (one per pair), no merge
+    (2, 200, 640, 37, 40, False),     # 200 rows of 256 per unit: padded rows clipped by the store
+])
+def test_attention_writes_p_y_like_the_se3_kernel(cuda, B, Lq, Lk, H, fs, with_rope):
+    """rw_attn_fwd_prope: the attention output y is bit-identical to rw_attn_fwd's
+    and the P y it writes beside y bit-identical to rw_se3_block_apply on that y,
+    through both output paths (the kernel's epilogue and the merge of key-split
+    units), twice in a row into [y | P y] rows as the self-attention drop-in uses."""
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table
+    from reworld_b200 import _native as nat
+    g = torch.Generator(device=cuda).manual_seed(Lq + H)
+    q = torch.randn(B, Lq, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
+    frames = Lq // fs
+    ctx = _poses(B, frames, torch.Generator().manual_seed(7)).to(torch.bfloat16)
+    mats = ctx.float().contiguous().to(cuda)
+    rope = None
+    if with_rope:
+        rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), cuda), (3, 22, 40), 9)
+    y_ref = chunk_attention(q, k, v, rope=rope)
+    py_ref = torch.empty_like(y_ref)
+    lib = nat.lib()
+    code = lib.rw_se3_block_apply(nat.c_vp(y_ref.data_ptr()), nat.c_vp(py_ref.data_ptr()), nat.c_vp(mats.data_ptr()),
+                                  B, Lq, H, 128, fs, *y_ref.stride()[:3], *py_ref.stride()[:3], nat.stream_ptr(cuda))
+    nat.check(code, "rw_se3_block_apply")
+    C = H * 128
+    for call in range(2):
+        yy = torch.full((B, Lq, 2 * C), float("nan"), dtype=torch.bfloat16, device=cuda)
+        y = yy[..., :C].view(B, Lq, H, 128)
+        py = yy[..., C:].view(B, Lq, H, 128)
+        chunk_attention(q, k, v, rope=rope, out=y, se3=(mats, fs, py))
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ref), call
+        assert torch.equal(py, py_ref), call
+    nat.check_status(cuda)
+
+
+def test_attention_prope_rejects_bad_frames(cuda):
+    from reworld_b200 import chunk_attention
+    q = torch.zeros(1, 100, 2, 128, dtype=torch.bfloat16, device=cuda)
+    k = torch.zeros(1, 256, 2, 128, dtype=torch.bfloat16, device=cuda)
+    po = torch.empty_like(q)
+    with pytest.raises(ValueError):       # 100 tokens are not whole frames of 30
+        chunk_attention(q, k, k, se3=(torch.zeros(1, 3, 4, 4, device=cuda), 30, po))
+    with pytest.raises(ValueError):       # fp16 matrices
+        chunk_attention(q, k, k, se3=(torch.zeros(1, 5, 4, 4, dtype=torch.float16, device=cuda), 20, po))
