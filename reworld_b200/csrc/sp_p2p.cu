@@ -46,11 +46,12 @@ struct ScatterQKV {
 };
 
 constexpr int SCATTER_THREADS = 128;  // a multiple of 16 (see scatter_qkv_kernel)
+constexpr int SCATTER_HSTEP = SCATTER_THREADS / 16;  // heads between two chunks of a thread
+constexpr int SCATTER_NB = 3;                         // chunks per thread and batch (24 heads: one batch)
 
-// CTAs walk this rank's tokens s; a thread handles the token's chunks
-// threadIdx.x, threadIdx.x + 128, ..., all at chunk position c16 =
-// threadIdx.x mod 16 of their head, so its 4 RoPE table entries are looked up
-// once per token.
+// CTAs walk this rank's tokens s; thread x handles chunk c16 = x mod 16 of heads
+// x / 16, x / 16 + 8, ..., so its 4 RoPE table entries are looked up once per
+// token, and the loads of a batch of heads are issued before its first store.
 __global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
   __shared__ int go;
   if (p.sync_on && p.sync.wait_epoch > 0) {
@@ -62,41 +63,57 @@ __global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __gr
       return;
     }
   }
-  const int nch = p.H * 16;
   const int c16 = threadIdx.x & 15;
+  const int h0 = threadIdx.x >> 4;
   const long long eoff = (long long)c16 * 8;
   for (int s = blockIdx.x; s < p.Ls; s += gridDim.x) {
     const int t = p.rank * p.Ls + s;
-    double2 cs[4];
-    float2 dl[4];
-    bool rot = false, has_d = false;
-    if (p.rope_on) {
-      const RopeToken rt = rope_token(p.rope, t, 0);
-      rot = rt.on;
-      has_d = rt.dl != nullptr;
+    const uint8_t* qrow = p.q + 2 * (s * p.q_sl + eoff);
+    const uint8_t* krow = p.k + 2 * (s * p.k_sl + eoff);
+    const uint8_t* vrow = p.v + 2 * (s * p.v_sl + eoff);
+    for (int hb = h0; hb < p.H; hb += SCATTER_HSTEP * SCATTER_NB) {
+      uint4 qv[SCATTER_NB], kv[SCATTER_NB], vv[SCATTER_NB];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        cs[j] = rope_freq(4 * c16 + j, rt);
-        dl[j] = has_d ? rt.dl[4 * c16 + j] : make_float2(0.f, 0.f);
+      for (int j = 0; j < SCATTER_NB; ++j) {
+        const long long h = hb + j * SCATTER_HSTEP;
+        if (h < p.H) {
+          qv[j] = __ldg(reinterpret_cast<const uint4*>(qrow + 2 * h * p.q_sh));
+          kv[j] = __ldg(reinterpret_cast<const uint4*>(krow + 2 * h * p.k_sh));
+          vv[j] = __ldg(reinterpret_cast<const uint4*>(vrow + 2 * h * p.v_sh));
+        }
       }
-    }
-    for (int c = threadIdx.x; c < nch; c += SCATTER_THREADS) {
-      const int h = c >> 4;
-      const int owner = h / p.Hp, hl = h - owner * p.Hp;
-      const uint4 qv = __ldg(reinterpret_cast<const uint4*>(p.q + 2 * (s * p.q_sl + h * p.q_sh + eoff)));
-      uint4 kv = __ldg(reinterpret_cast<const uint4*>(p.k + 2 * (s * p.k_sl + h * p.k_sh + eoff)));
-      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(p.v + 2 * (s * p.v_sl + h * p.v_sh + eoff)));
-      if (rot) {
-        kv.x = rope_rotate(kv.x, cs[0], has_d, dl[0]);
-        kv.y = rope_rotate(kv.y, cs[1], has_d, dl[1]);
-        kv.z = rope_rotate(kv.z, cs[2], has_d, dl[2]);
-        kv.w = rope_rotate(kv.w, cs[3], has_d, dl[3]);
+      double2 cs[4];
+      float2 dl[4];
+      bool rot = false, has_d = false;
+      if (p.rope_on) {
+        const RopeToken rt = rope_token(p.rope, t, 0);
+        rot = rt.on;
+        has_d = rt.dl != nullptr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          cs[j] = rope_freq(4 * c16 + j, rt);
+          dl[j] = has_d ? rt.dl[4 * c16 + j] : make_float2(0.f, 0.f);
+        }
       }
-      const long long qoff = 2 * (((long long)t * p.Hp + hl) * 128 + eoff);
-      const long long coff = 2 * (((long long)(p.dst_start + t) * p.Hp + hl) * 128 + eoff);
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.q_dst[owner]) + qoff) = qv;
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ck_dst[owner]) + coff) = kv;
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv;
+#pragma unroll
+      for (int j = 0; j < SCATTER_NB; ++j) {
+        const int h = hb + j * SCATTER_HSTEP;
+        if (h < p.H) {
+          const int owner = h / p.Hp, hl = h - owner * p.Hp;
+          uint4 kr = kv[j];
+          if (rot) {
+            kr.x = rope_rotate(kr.x, cs[0], has_d, dl[0]);
+            kr.y = rope_rotate(kr.y, cs[1], has_d, dl[1]);
+            kr.z = rope_rotate(kr.z, cs[2], has_d, dl[2]);
+            kr.w = rope_rotate(kr.w, cs[3], has_d, dl[3]);
+          }
+          const long long qoff = 2 * (((long long)t * p.Hp + hl) * 128 + eoff);
+          const long long coff = 2 * (((long long)(p.dst_start + t) * p.Hp + hl) * 128 + eoff);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.q_dst[owner]) + qoff) = qv[j];
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ck_dst[owner]) + coff) = kr;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.cv_dst[owner]) + coff) = vv[j];
+        }
+      }
     }
   }
   if (p.sync_on && p.sync.signal_epoch > 0) sp_signal_done(p.sync);
