@@ -184,17 +184,22 @@ class Rollout:
         frames = random_walk(512 * FRAMES, seed=0, step_t=0.1 / FRAMES, step_deg=5.0 / FRAMES,
                              revisit_every=REVISIT_EVERY * FRAMES)
         self.frame_ctx = torch.from_numpy(np.stack(frames)).to(device).unsqueeze(0)
+        self.frame_ctx_host = self.frame_ctx.cpu()   # the camera path is host input: poses need no device read
+        self._pose = None
         self.launches = 0
         self.flops_all = 0.0          # attention FLOPs of all heads issued so far (whole job)
         self.host_issue_s = []        # host time to enqueue each forward (30 layers of launches)
         self.scatter_events = []      # Ulysses: event pairs around each layer's q/k/v scatter
         self._split_cache = {}
         self.attn_events = []
+        self.step_marks = []          # per timed step: events at each forward's start, the bank update's start and end
+        self.bank_host_s = []         # host time of each bank update (its decision is read back to the host)
 
     def new_bank(self):
         """A cold bank (budget split of the v15b knobs) and an empty cache."""
         from reworld_b200.landmark import LandmarkBankStack
         self.bank = None
+        self._pose = None
         torch.cuda.empty_cache()
         self.bank = LandmarkBankStack.from_budget(CT, N_LAYERS, self.H, HEAD_DIM, BUDGET_CHUNKS, SINK_KNOB,
                                                   RECENT_CAP, LANDMARK_K, POLICY, cache_tokens=self.cap,
@@ -210,10 +215,20 @@ class Rollout:
                 self.cache_v[l][:, self.tot:self.tot + CT].normal_()
             self.bank_update()
 
+    def prepare_bank(self):
+        """The chunk's pose and its bank decision, queued before the chunk's forwards
+        (the decision depends on poses only), so the update after them does not wait
+        for the device to drain."""
+        from reworld_b200.landmark import chunk_pose
+        c = self.chunk
+        self._pose = chunk_pose(self.frame_ctx_host[:, :(c + 1) * FRAMES], FRAMES)
+        self.bank.prepare(self._pose, self._pose)
+
     def bank_update(self):
         from reworld_b200.landmark import chunk_pose
         c = self.chunk
-        pose = chunk_pose(self.frame_ctx[:, :(c + 1) * FRAMES], FRAMES)
+        pose = self._pose if self._pose is not None else chunk_pose(self.frame_ctx_host[:, :(c + 1) * FRAMES], FRAMES)
+        self._pose = None
         src_k = [ck[0, self.tot:self.tot + CT] for ck in self.cache_k]
         src_v = [cv[0, self.tot:self.tot + CT] for cv in self.cache_v]
         R = self.bank.add_chunk_from(src_k, src_v, pose, pose)
@@ -262,11 +277,25 @@ class Rollout:
         return self._split_cache[key]
 
     def step(self, time_attn=False):
+        marks = [] if time_attn else None
+        self.prepare_bank()
         for _ in range(FORWARDS_PER_CHUNK):
             t0 = time.perf_counter()
+            if marks is not None:
+                marks.append(torch.cuda.Event(enable_timing=True))
+                marks[-1].record()
             self.forward(time_attn)
             self.host_issue_s.append(time.perf_counter() - t0)
+        if marks is not None:
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+        t0 = time.perf_counter()
         self.bank_update()
+        if marks is not None:
+            self.bank_host_s.append(time.perf_counter() - t0)
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+            self.step_marks.append(marks)
 
 
 def run_gpu(args):
@@ -295,6 +324,8 @@ def run_gpu(args):
     ro.attn_events.clear()
     ro.host_issue_s.clear()
     ro.scatter_events.clear()
+    ro.step_marks.clear()
+    ro.bank_host_s.clear()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         torch.cuda.synchronize()
@@ -318,6 +349,19 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
 
+    # where a step's time goes (device clock on this rank): the forwards and the bank update
+    fwd_ms = [m[i].elapsed_time(m[i + 1]) for m in ro.step_marks for i in range(FORWARDS_PER_CHUNK)]
+    bank_ms = [m[-2].elapsed_time(m[-1]) for m in ro.step_marks]
+    breakdown = {"forward_ms": round(statistics.median(fwd_ms), 3),
+                 "layer_us": round(1e3 * statistics.median(fwd_ms) / N_LAYERS, 1),
+                 "attention_us": round(1e3 * statistics.median(a.elapsed_time(b) for a, b, _ in ro.attn_events), 1),
+                 "bank_update_ms": round(statistics.median(bank_ms), 3),
+                 "bank_update_host_ms": round(1e3 * statistics.median(ro.bank_host_s), 3),
+                 "note": "medians over the timed steps on rank 0; a layer = " +
+                         ("scatter + attention (+ merge) + launch gaps" if world > 1 else
+                          "RoPE store + attention (+ merge)") +
+                         "; bank update = pack of the chunk, gather of all layers' caches (its decision was "
+                         "queued before the forwards and is read back without draining the device)"}
     exchange = None
     if world > 1:
         # the seq->head exchange of one layer: bytes this rank's scatter sends over NVLink
@@ -374,8 +418,10 @@ def run_gpu(args):
             line["e2e"] = e2e
         if parity is not None:
             line["sp_parity"] = parity
+        line["step_breakdown"] = breakdown
         if exchange is not None:
             line["exchange"] = exchange
+            breakdown["scatter_us"] = exchange["scatter_us"]
         line["rollout_cold32"] = cold
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
@@ -414,6 +460,7 @@ def run_e2e(ro, args, dev):
 
     def step():
         n = 0
+        ro.prepare_bank()
         for _f in range(FORWARDS_PER_CHUNK):
             start_frame = (ro.chunk * CT) // (TOK_H * TOK_W)
             rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)
@@ -564,6 +611,7 @@ def run_e2e_sp(ro, args, dev):
 
     def step():
         n = 0
+        ro.prepare_bank()
         for _f in range(FORWARDS_PER_CHUNK):
             start_frame = (ro.chunk * CT) // (TOK_H * TOK_W)
             rope = ro.RopeArgs(ro.table, (FRAMES, TOK_H, TOK_W), start_frame % 1000)

@@ -160,6 +160,12 @@ class DeviceBankDecisions:
     def step(self, admit=None, target=None):
         """admit = (pose, born, slot) or None; target = pose for mode 'b'.
         Returns (evicted [(born, slot)], R, R_slots)."""
+        return self.collect(self.issue(admit, target))
+
+    def issue(self, admit=None, target=None):
+        """Queues the decision (rw_bank_step) and the copy of its result to pinned
+        host memory without waiting for either; returns the ticket that collect()
+        turns into step()'s result.  Tickets are collected in the order issued."""
         recs = (RwPose * 2)()
         if admit is not None:
             recs[0] = pose_record(admit[0])
@@ -180,7 +186,18 @@ class DeviceBankDecisions:
                 c_vp(p0 + ps) if target is not None else None, self.retrieve_k, self.mode,
                 c_vp(self.result.data_ptr()), _native.stream_ptr(self.device))
         _native.check(code, "rw_bank_step")
-        res = RwBankResult.from_buffer_copy(self.result.cpu().numpy().tobytes())
+        host_res = torch.empty(self.result.numel(), dtype=torch.uint8, pin_memory=True)
+        host_res.copy_(self.result, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        return host_res, done, admit
+
+    def collect(self, ticket):
+        """Waits for an issued decision (only for it and the work queued before it)
+        and applies it to the host mirror; returns (evicted, R, R_slots)."""
+        host_res, done, admit = ticket
+        done.synchronize()
+        res = RwBankResult.from_buffer_copy(host_res.numpy().tobytes())
         evicted = [(res.evicted_born[i], res.evicted_slot[i]) for i in range(min(res.n_evicted, 4))]
         if res.n_evicted > 4:
             raise RuntimeError("more than 4 evictions in one step")
@@ -474,6 +491,7 @@ class LandmarkBankStack:
         self.sink, self.recent, self.bank = [], [], []
         self.events = []
         self._n = 0
+        self._pending = None   # a decision queued by prepare() for chunk self._n
 
     @classmethod
     def from_budget(cls, chunk_tokens, n_layers, num_heads, head_dim, budget_chunks, n_sink=1, recent_w=5,
@@ -488,6 +506,26 @@ class LandmarkBankStack:
         return st
 
     # -- chunk admission ----------------------------------------------------
+    def _aging_out(self):
+        """The recent-window entry that leaves the window when the next chunk joins."""
+        if self._n < self.n_sink or len(self.recent) + 1 <= self.recent_w:
+            return None
+        return self.recent[0]
+
+    def prepare(self, pose, pose_next=None):
+        """Queues the bank decision of the next add_chunk_from (same pose and
+        pose_next) ahead of time: the decision depends only on poses and bank
+        membership, not on the chunk's K/V, so it can run before the forwards that
+        produce them, and add_chunk_from then finds its result on the host instead
+        of waiting for the device to drain.  Optional; the results are the same."""
+        if self._pending is not None:
+            raise RuntimeError("a prepared bank decision is still pending")
+        admit = self._aging_out()
+        target = pose_next if pose_next is not None else pose
+        ticket = self.dec.issue(admit=(admit.pose, admit.born, admit.slot) if admit is not None else None,
+                                target=target if self.mode == "b" else None)
+        self._pending = (self._n, bytes(pose_record(target)), admit, ticket)
+
     def add_chunk_from(self, src_k, src_v, pose, pose_next=None):
         """src_k/src_v: per-layer lists of [ct, H, D] views (e.g. the cache rows
         the chunk was just written to).  Packs them into a pool slot (one launch)
@@ -515,9 +553,16 @@ class LandmarkBankStack:
                     raise RuntimeError("more than one chunk aged out in one step")
                 admit = old
         target = pose_next if pose_next is not None else pose
-        evicted, R, _ = self.dec.step(
-            admit=(admit.pose, admit.born, admit.slot) if admit is not None else None,
-            target=target if self.mode == "b" else None)
+        if self._pending is not None:
+            pc, ptarget, padmit, ticket = self._pending
+            self._pending = None
+            if pc != c or padmit is not admit or ptarget != bytes(pose_record(target)):
+                raise RuntimeError("the prepared bank decision was for another chunk or pose")
+            evicted, R, _ = self.dec.collect(ticket)
+        else:
+            evicted, R, _ = self.dec.step(
+                admit=(admit.pose, admit.born, admit.slot) if admit is not None else None,
+                target=target if self.mode == "b" else None)
         for born, slot_ev in evicted:
             j = [m.born for m in self.bank].index(born)
             self.bank.pop(j)

@@ -130,9 +130,12 @@ def test_bank_decisions_and_cache_bytes_vs_reference(cuda, golden, name):
     _status_clean()
 
 
-def test_bank_stack_all_layers_one_launch(cuda):
+@pytest.mark.parametrize("prepared", [False, True])
+def test_bank_stack_all_layers_one_launch(cuda, prepared):
     """The all-layers stack makes the same decisions as the oracle and assembles
-    every layer's cache from that layer's own chunk K/V."""
+    every layer's cache from that layer's own chunk K/V — also when each chunk's
+    decision is queued by prepare() before its K/V exist (as the rollout does,
+    ahead of the chunk's forwards)."""
     from reworld_b200.landmark import LandmarkBankStack
     from reworld_b200.poses import random_walk
     ct, H, D, L = 4, 2, 128, 5
@@ -143,6 +146,8 @@ def test_bank_stack_all_layers_one_launch(cuda):
     data = {}
     caps = [torch.zeros(1, 8 * ct, H, D, dtype=torch.bfloat16, device=cuda) for _ in range(2 * L)]
     for c in range(len(poses) - 1):
+        if prepared:
+            st.prepare(poses[c], poses[c + 1])
         kvs = torch.randn(L, 2, ct, H, D, generator=gen, device=cuda).to(torch.bfloat16)
         data[c] = kvs
         R = st.add_chunk_from([kvs[l, 0] for l in range(L)], [kvs[l, 1] for l in range(L)], poses[c], poses[c + 1])
@@ -155,6 +160,10 @@ def test_bank_stack_all_layers_one_launch(cuda):
             want_k = torch.cat([data[b][l, 0] for b in lay])
             want_v = torch.cat([data[b][l, 1] for b in lay])
             assert torch.equal(caps[l][0, :tot], want_k) and torch.equal(caps[L + l][0, :tot], want_v)
+    if prepared:
+        st.prepare(poses[0], poses[1])
+        with pytest.raises(RuntimeError):   # a decision prepared for other poses is refused
+            st.add_chunk_from([kvs[l, 0] for l in range(L)], [kvs[l, 1] for l in range(L)], poses[2], poses[3])
     _status_clean()
 
 
