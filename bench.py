@@ -710,6 +710,7 @@ def gpu_side_baselines(ro, dev):
     out["rope_kv_store"] = store_measure(ro, dev, timeit)
     out["qkv_norm_rope_store"] = qkv_norm_measure(ro, dev, timeit)
     out["se3_block_apply"] = se3_measure(ro, dev, timeit)
+    out["streaming_scale"] = streaming_scale(dev)
     out["host_tier"] = host_tier_measure(dev)
     # the DiT block's text cross-attention: the chunk's queries over 512 cached text keys
     kt = torch.randn(1, 512, HEADS, HEAD_DIM, device=dev).to(torch.bfloat16)
@@ -1172,6 +1173,64 @@ def qkv_norm_measure(ro, dev, timeit, n_rot=4):
             "unfused": "torch WanRMSNorm formula on q and k (GPU) + rw_rope_kv_store",
             "timing": f"CUDA graph of {n_rot} launches over {n_rot} layers' inputs and caches, replayed; "
                       "per launch"}
+
+
+def streaming_scale(dev, batches=(1, 2, 4, 8)):
+    """The two streaming kernels of a layer-chunk over 1..8 chunks at once (batch
+    B): time = a fixed part per launch + a part per chunk; the per-chunk slope's
+    bandwidth is what the inner loop streams at.  CUDA-graph replay, inputs
+    rotating over two copies (each > L2 from B = 2 on)."""
+    from reworld_b200 import RopeArgs, build_freqs, device_table, qkv_norm_rope_store, rope_kv_store
+    C = HEADS * HEAD_DIM
+    g = torch.Generator(device=dev).manual_seed(5)
+    rope = RopeArgs(device_table(build_freqs(HEAD_DIM, 12 / 22, 20 / 40), dev), (FRAMES, TOK_H, TOK_W), 36)
+    wq = (1 + 0.05 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    res = {"norm_us": [], "store_us": []}
+    for B in batches:
+        x = [(torch.randn(B, CT, 3 * C, generator=g, device=dev) * 1.5).to(torch.bfloat16) for _ in range(2)]
+        ck = [torch.zeros(B, 2 * CT, HEADS, HEAD_DIM, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        cv = [torch.zeros_like(c) for c in ck]
+        qo = [torch.empty(B, CT, HEADS, HEAD_DIM, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        fns = {"norm_us": lambda i: qkv_norm_rope_store(x[i][..., :C], x[i][..., C:2 * C], x[i][..., 2 * C:], wq, wq,
+                                                         ck[i], cv[i], CT, 1e-6, rope=rope, q_out=qo[i]),
+               "store_us": lambda i: rope_kv_store(x[i][..., C:2 * C].view(B, CT, HEADS, HEAD_DIM),
+                                                   x[i][..., 2 * C:].view(B, CT, HEADS, HEAD_DIM), ck[i], cv[i], CT,
+                                                   rope=rope)}
+        for key, fn in fns.items():
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fn(0)
+                fn(1)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn(0)
+                fn(1)
+            ts = []
+            for _ in range(5):
+                for _ in range(2):
+                    gr.replay()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                a.record()
+                for _ in range(10):
+                    gr.replay()
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b) / 20)
+            res[key].append(round(1e3 * sorted(ts)[2], 2))
+        del x, ck, cv, qo
+    _, _, hbm, _ = load_peaks()
+    for key, nb in (("norm", CT * C * 12), ("store", CT * C * 8)):
+        t = res[f"{key}_us"]
+        slope = (t[-1] - t[0]) / (batches[-1] - batches[0])
+        res[f"{key}_slope_gbs"] = round(nb / (slope * 1e-6) / 1e9, 1)
+        res[f"{key}_slope_frac_of_hbm"] = round(nb / (slope * 1e-6) / 1e9 / hbm, 3)
+        res[f"{key}_fixed_us"] = round(t[0] - slope, 2)
+    res["batches"] = list(batches)
+    res["bytes_per_chunk"] = {"norm": CT * C * 12, "store": CT * C * 8}
+    return res
 
 
 # ------------------------------------------------------------------ CPU baseline / reference arm
