@@ -135,8 +135,14 @@ struct Work {
   bool shared;
 };
 
+// Units of fewer key tiles than this run whole even with a workspace: for short
+// key ranges the merge launch and the partial results' traffic cost more than the
+// idle pairs of a partial last wave (24 heads x 2640 queries: 512 keys 43.9 us
+// whole vs 54.2 split, 2640 keys 100 vs 106, 5280 keys (42 tiles) 163 vs 163).
+constexpr int SPLIT_MIN_KV = 43;
+
 inline Work work_for(int units, int n_kv, int resident, bool have_workspace) {
-  if (!have_workspace || resident < 1) return Work{units, false};
+  if (!have_workspace || resident < 1 || n_kv < SPLIT_MIN_KV) return Work{units, false};
   int Np = resident;
   if ((long long)units * n_kv < Np) Np = units * n_kv;  // all of it is tail: one tile per pair at least
   if (units % Np == 0) return Work{units, false};        // whole waves only

@@ -168,7 +168,7 @@ def test_attention_full_size_heads_vs_fp32_reference(cuda):
 
 
 @pytest.mark.parametrize("B,Lq,Lk,H", [(1, 2640, 34320, 24), (1, 2640, 34320, 6), (1, 2640, 34320, 3),
-                                         (1, 660, 2640, 40), (2, 300, 1000, 2)])
+                                         (1, 660, 5600, 40), (2, 300, 6000, 2)])
 def test_attention_key_split_matches_unsplit(cuda, B, Lq, Lk, H):
     """Pairs sharing units (workspace given: equal shares of the key tiles, partial
     results merged) and one whole unit per pair (no workspace) compute the same
