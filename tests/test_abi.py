@@ -114,6 +114,8 @@ def test_attn_workspace_plan():
     # 704x1280 chunk over the 13-chunk cache: 264 query-pair units, a split tail
     n = lib.rw_attn_workspace_bytes(1, 2640, 34320, 24)
     assert n > 0 and n % (4 * (128 * 256 + 512)) == 0
+    # short key ranges run whole: no workspace (text cross-attention, 512 keys)
+    assert lib.rw_attn_workspace_bytes(1, 2640, 512, 24) == 0
     assert lib.rw_attn_workspace_bytes(0, 1, 1, 1) == 0
 
 
