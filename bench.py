@@ -381,6 +381,7 @@ def run_gpu(args):
     # e2e: host buffers through the public API, copies inside the timed region
     e2e = run_e2e(ro, args, dev) if world == 1 else run_e2e_sp(ro, args, dev)
     parity = sp_parity(ro, dev, world, rank, group) if world > 1 else None
+    stress_sp = stress_sp_measure(dev, world, rank, group) if world > 1 else None
 
     step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
@@ -418,6 +419,8 @@ def run_gpu(args):
             line["e2e"] = e2e
         if parity is not None:
             line["sp_parity"] = parity
+        if stress_sp is not None:
+            line["stress_b4_sp"] = stress_sp
         line["step_breakdown"] = breakdown
         if exchange is not None:
             line["exchange"] = exchange
@@ -778,6 +781,60 @@ def stress_measure(dev, calls=4):
     res["note"] = ("batch 4 x 24 heads is the whole stress layer on one GPU; 3 heads is one rank's share at "
                    "8 GPUs; decision time = pack + rw_bank_step + host readback of one chunk, full bank")
     return res
+
+
+def stress_sp_measure(dev, world, rank, group, n_layers=2, steps=3):
+    """The stress configuration at N GPUs: four rollouts (batch 4) of one 2640-token
+    chunk each, every one through the Ulysses layer (q/k/v scatter with k's RoPE and
+    the cache write, attention of this rank's heads over the 24-chunk budget plus the
+    chunk = 66000 keys, output rows to their owners), over head-sharded caches; one
+    cache per (rollout, layer), n_layers layers per step.  Device time per layer of
+    all four rollouts, max over ranks (a barrier on both sides of the timed steps)."""
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, device_table
+    from reworld_b200.landmark import budget_split
+    from reworld_b200.ulysses import UlyssesP2P
+    sp = budget_split(24, 1, 7, 120, "v15b")
+    lk = (sp.budget + 1) * CT
+    B = 4
+    u = UlyssesP2P(group, B * n_layers, lk, CT, HEADS, HEAD_DIM, device=dev)
+    g = torch.Generator(device=dev).manual_seed(900 + rank)
+    for i in range(B * n_layers):
+        u.caches[i].normal_(generator=g)
+    Ls = CT // world
+    x = [[torch.randn(1, Ls, HEADS, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+         for _ in range(B)]
+    rope = RopeArgs(device_table(build_freqs(HEAD_DIM, 12 / 22, 20 / 40), dev), (FRAMES, TOK_H, TOK_W), 36)
+
+    def step():
+        for l in range(n_layers):
+            for b in range(B):
+                u.layer(b * n_layers + l, x[b][0], x[b][1], x[b][2], lk - CT, rope=rope, sync_output=False)
+
+    step()
+    step()
+    u.finish()
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    u.finish()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / (steps * n_layers)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    ms = float(t.item())
+    dist.barrier(group=group)
+    del u
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    return {"workload": f"stress: batch 4 rollouts x 2640 tokens, budget 24 = {sp.n_sink} sink + {sp.recent_w} recent "
+                        f"+ {sp.n_landmark} landmarks (bank K {sp.K}) + the chunk = {lk} keys, 24 heads sharded "
+                        f"{HEADS // world} per rank, each rollout through the Ulysses layer",
+            "ms_per_layer": round(ms, 4), "tflops": round(B * attn_flops(CT, lk, HEADS) / ms / 1e9, 1),
+            "n_gpus": world, "layers_timed": steps * n_layers}
 
 
 def gemm_ab(dev, reps=9, calls=8, n_inputs=3):
