@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(128)
                    long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
                    const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0,
                    const __grid_constant__ rw_sp_sync_t sync, int sync_signal, const __grid_constant__ Se3Out se3) {
+  griddep_wait();  // launched as a programmatic dependent of the attention: its slots are complete
   combine_unit(scratch, out, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, U, Np, scale_log2, peer_ptrs, peer_Ls, peer_H,
                peer_h0, se3);
   if (sync_signal) sp_signal_done(sync);  // every merged row is at its owner rank
@@ -227,10 +228,23 @@ int attn_run(const void* q, const void* k, const void* v, void* o, int B, int Lq
     const int tail_units = units - (units / wk.Np) * wk.Np;
     rw_sp_sync_t none{};
     const bool sig = peer.sync != nullptr && peer.sync->signal_epoch > 0;
-    attn::combine_kernel<<<dim3(tail_units, 2, attn::HD / attn::COMBINE_COLS), 128, 0, (cudaStream_t)stream>>>(
-        (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, units, wk.Np, scale_log2,
-        peer.ptrs, peer.Ls, peer.H, peer.h0, sig ? *peer.sync : none, sig ? 1 : 0, se3);
-    if (cudaGetLastError() != cudaSuccess) return RW_ERR_CUDA;
+    // a programmatic dependent of the attention (its blocks start as the pairs finish
+    // and wait for the whole attention grid before reading the slots)
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(tail_units, 2, attn::HD / attn::COMBINE_COLS);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const rw_sp_sync_t sy = sig ? *peer.sync : none;
+    if (cudaLaunchKernelEx(&cfg, attn::combine_kernel, (const float*)workspace, (uint8_t*)o, o_sb, o_sl, o_sh, Lq, H,
+                           nqp, n_kv, units, wk.Np, scale_log2, peer.ptrs, peer.Ls, peer.H, peer.h0, sy,
+                           sig ? 1 : 0, se3) != cudaSuccess)
+      return RW_ERR_CUDA;
   }
   return RW_OK;
 }

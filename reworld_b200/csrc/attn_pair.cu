@@ -292,6 +292,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   if (warp == WARP_LOAD) {
     // ------------------------------------------------------------ producer (both CTAs)
     setmaxnreg_dec<REG_OTHER>();
+    // launched as a programmatic dependent: the previous kernel (the cache write) has
+    // finished and its rows are visible before the first load; every global access of
+    // this kernel follows these loads
+    if (lane == 0) griddep_wait();
+    __syncwarp();
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -710,6 +715,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     while (globaltimer_ns() - t0 < 200000ull) {
     }
   }
+  if (threadIdx.x == 0) griddep_launch_dependents();  // the merge kernel may start its prologue
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA of the pair leaves while the other may still touch its memory or TMEM
@@ -804,8 +810,25 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   }
   if (Np < 1 || U < 1 || 2LL * Np > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
   if (U % Np != 0 && (long long)(U % Np) * ((Lk + BN - 1) / BN) < Np) return RW_ERR_INVALID_ARG;  // empty tail shares
-  attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, mpo, prm);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  if (peer_ptrs != nullptr) {
+    // sequence-parallel layer: ordered by its own cross-rank waits, launched normally
+    attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, mpo, prm);
+    return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  }
+  // a programmatic dependent of the previous kernel on the stream: the pairs' setup
+  // (barriers, TMEM, descriptors) overlaps that kernel's last wave; the producer waits
+  // for it before the first load
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(2 * Np), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_pair_kernel, mq, mk, mv, mo, mpo, prm) == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
 
 }  // namespace pair

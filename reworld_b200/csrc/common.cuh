@@ -26,6 +26,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic stream
+// serialization attribute may start before the previous kernel on its stream has
+// finished: griddep_wait() blocks the calling thread until that kernel has completed
+// and its memory is visible (a no-op in a normally launched kernel), and
+// griddep_launch_dependents() lets such a dependent kernel start early (a no-op when
+// none follows).  A dependent kernel must not touch global memory that the previous
+// kernel reads or writes before its griddep_wait().
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

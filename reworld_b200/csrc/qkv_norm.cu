@@ -135,6 +135,7 @@ __device__ __forceinline__ bool pair_bar_or(int id, bool pred) {
 }
 
 __global__ void __launch_bounds__(MAX_SLOTS * 64, 1) qkv_norm_kernel(const __grid_constant__ Params p) {
+  griddep_launch_dependents();  // the attention that reads q and these rows may start its prologue now
   extern __shared__ __align__(128) uint8_t stage_mem[];
   __shared__ __align__(8) uint64_t full[MAX_SLOTS];
   __shared__ float2 red[MAX_SLOTS][2];  // [slot][half]: (sum q^2, sum k^2) of each warp

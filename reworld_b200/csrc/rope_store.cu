@@ -70,6 +70,7 @@ __device__ __forceinline__ uint4 rotate(uint4 v, const RopeRegs& r) {
 // token (then one add per head).  The loads of a batch of NB heads are all issued
 // before the batch's first store, so one round trip to memory covers them.
 __global__ void __launch_bounds__(THREADS, 4) rope_kv_store_kernel(const __grid_constant__ Params p) {
+  griddep_launch_dependents();  // the attention that reads these rows may start its prologue now
   const uint32_t tokens = (uint32_t)p.B * (uint32_t)p.L;  // < 2^31 (host check)
   const int c16 = threadIdx.x & 15;
   const int h0 = threadIdx.x >> 4;
