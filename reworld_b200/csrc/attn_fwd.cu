@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(128)
                    long long o_sh, int Lq, int H, int nqp, int n_kv, int U, int Np, float scale_log2,
                    const unsigned long long* __restrict__ peer_ptrs, int peer_Ls, int peer_H, int peer_h0,
                    const __grid_constant__ rw_sp_sync_t sync, int sync_signal, const __grid_constant__ Se3Out se3) {
+  griddep_launch_dependents();  // the next kernel may be scheduled; it waits for this one
   griddep_wait();  // launched as a programmatic dependent of the attention: its slots are complete
   combine_unit(scratch, out, o_sb, o_sl, o_sh, Lq, H, nqp, n_kv, U, Np, scale_log2, peer_ptrs, peer_Ls, peer_H,
                peer_h0, se3);

@@ -190,6 +190,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     tmem_alloc_pair(&sb.tmem_base, C::TMEM_COLS);
     tmem_relinquish_pair();
   }
+  griddep_launch_dependents();  // the next kernel may be scheduled; it waits for this one
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs (A, the residual) are complete
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
@@ -533,8 +535,10 @@ int launch(const void* A, long long lda, const void* B, long long ldb, const voi
   prm.C = reinterpret_cast<__nv_bfloat16*>(Cm);
   prm.ldc = ldc;
   prm.status = status;
-  gemm_pair_kernel<BN><<<(unsigned)(2 * prm.Np), NUM_THREADS, Cfg<BN>::SMEM_BYTES, stream>>>(ma, mb, mc, prm);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  return launch_dependent(gemm_pair_kernel<BN>, dim3((unsigned)(2 * prm.Np)), dim3(NUM_THREADS),
+                          (size_t)Cfg<BN>::SMEM_BYTES, stream, ma, mb, mc, prm) == cudaSuccess
+             ? RW_OK
+             : RW_ERR_CUDA;
 }
 
 }  // namespace gemm

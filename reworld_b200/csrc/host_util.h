@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 namespace rw {
 
@@ -102,3 +103,22 @@ inline bool ensure_smem_attr(const void* func, int bytes, std::atomic<unsigned l
 inline bool stride_ok(long long s) { return s > 0 && (s % 8) == 0 && s < (1ll << 38); }
 
 }  // namespace rw
+
+// Launches `kernel` as a programmatic dependent of the previous kernel on `stream`:
+// it may start while that kernel's last blocks run, and must call griddep_wait()
+// before it touches global memory (common.cuh).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                    Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

@@ -136,6 +136,7 @@ __device__ __forceinline__ bool pair_bar_or(int id, bool pred) {
 
 __global__ void __launch_bounds__(MAX_SLOTS * 64, 1) qkv_norm_kernel(const __grid_constant__ Params p) {
   griddep_launch_dependents();  // the attention that reads q and these rows may start its prologue now
+  griddep_wait();               // launched as a dependent: the previous kernel (the projection) is done
   extern __shared__ __align__(128) uint8_t stage_mem[];
   __shared__ __align__(8) uint64_t full[MAX_SLOTS];
   __shared__ float2 red[MAX_SLOTS][2];  // [slot][half]: (sum q^2, sum k^2) of each warp
@@ -344,6 +345,8 @@ extern "C" int rw_qkv_norm_rope_store(const void* q_in, const void* k_in, const 
     per_sm = 1;
   const long long total = (long long)B * L;
   const long long grid = total < (long long)sms * per_sm ? total : (long long)sms * per_sm;
-  qkvn::qkv_norm_kernel<<<(unsigned)grid, slots * 64, smem, (cudaStream_t)stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  return launch_dependent(qkvn::qkv_norm_kernel, dim3((unsigned)grid), dim3(slots * 64), (size_t)smem,
+                          (cudaStream_t)stream, p) == cudaSuccess
+             ? RW_OK
+             : RW_ERR_CUDA;
 }

@@ -71,6 +71,7 @@ __device__ __forceinline__ uint4 rotate(uint4 v, const RopeRegs& r) {
 // before the batch's first store, so one round trip to memory covers them.
 __global__ void __launch_bounds__(THREADS, 4) rope_kv_store_kernel(const __grid_constant__ Params p) {
   griddep_launch_dependents();  // the attention that reads these rows may start its prologue now
+  griddep_wait();               // launched as a dependent: the previous kernel is done
   const uint32_t tokens = (uint32_t)p.B * (uint32_t)p.L;  // < 2^31 (host check)
   const int c16 = threadIdx.x & 15;
   const int h0 = threadIdx.x >> 4;
@@ -177,6 +178,8 @@ extern "C" int rw_rope_kv_store(const void* k, const void* v, const void* q_in, 
   const long long tokens = (long long)B * L;
   const long long cap = (long long)sms * 16;  // resident 128-thread CTAs, tokens strided over them
   const long long grid = tokens < cap ? tokens : cap;
-  store::rope_kv_store_kernel<<<(unsigned)grid, store::THREADS, 0, (cudaStream_t)stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  return launch_dependent(store::rope_kv_store_kernel, dim3((unsigned)grid), dim3(store::THREADS), 0,
+                          (cudaStream_t)stream, p) == cudaSuccess
+             ? RW_OK
+             : RW_ERR_CUDA;
 }

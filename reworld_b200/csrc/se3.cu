@@ -31,6 +31,8 @@ struct Params {
 constexpr int THREADS = 64;  // small CTAs, one per token; a thread's 6 chunks (24 heads) unrolled
 
 __global__ void __launch_bounds__(THREADS) se3_kernel(const __grid_constant__ Params p) {
+  griddep_launch_dependents();
+  griddep_wait();  // launched as a dependent: the previous kernel is done
   const long long tokens = (long long)p.B * p.L;
   const int nch = p.H * 16;  // 16-byte chunks per token
   for (long long tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
@@ -89,6 +91,8 @@ extern "C" int rw_se3_block_apply(const void* x, void* out, const float* mats, i
   const long long tokens = (long long)B * L;
   const long long cap = (long long)sms * 20;  // tokens strided over at most 20 CTAs per SM
   const long long grid = tokens < cap ? tokens : cap;
-  se3::se3_kernel<<<(unsigned)grid, se3::THREADS, 0, (cudaStream_t)stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  return launch_dependent(se3::se3_kernel, dim3((unsigned)grid), dim3(se3::THREADS), 0, (cudaStream_t)stream, p) ==
+                 cudaSuccess
+             ? RW_OK
+             : RW_ERR_CUDA;
 }
