@@ -279,12 +279,14 @@ class Rollout:
     def step(self, time_attn=False):
         marks = [] if time_attn else None
         self.prepare_bank()
-        for _ in range(FORWARDS_PER_CHUNK):
+        for i in range(FORWARDS_PER_CHUNK):
             t0 = time.perf_counter()
             if marks is not None:
                 marks.append(torch.cuda.Event(enable_timing=True))
                 marks[-1].record()
-            self.forward(time_attn)
+            # per-launch events only in the first forward: an event between two kernels
+            # keeps the second from starting early (programmatic dependent launch)
+            self.forward(time_attn and i == 0)
             self.host_issue_s.append(time.perf_counter() - t0)
         if marks is not None:
             marks.append(torch.cuda.Event(enable_timing=True))

@@ -46,6 +46,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 template <int PER>
 __global__ void __launch_bounds__(THREADS) row_norm_kernel(const __grid_constant__ Params p) {
+  griddep_launch_dependents();
+  griddep_wait();  // launched as a dependent: the previous kernel is done
   __shared__ float red[THREADS / 32];
   const int nch = p.C / 8;
   const uint4* wv = reinterpret_cast<const uint4*>(p.w);
@@ -169,9 +171,11 @@ extern "C" int rw_row_norm(const void* x, void* out, const void* w, const void* 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long cap = (long long)sms * 16;  // 16 resident CTAs per SM, rows strided over them
   const long long grid = rows < cap ? rows : cap;
-  if (C <= 8 * 3 * rown::THREADS)
-    rown::row_norm_kernel<3><<<(unsigned)grid, rown::THREADS, 0, (cudaStream_t)stream>>>(p);
-  else
-    rown::row_norm_kernel<rown::MAX_PER><<<(unsigned)grid, rown::THREADS, 0, (cudaStream_t)stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  const cudaError_t e =
+      C <= 8 * 3 * rown::THREADS
+          ? launch_dependent(rown::row_norm_kernel<3>, dim3((unsigned)grid), dim3(rown::THREADS), 0,
+                             (cudaStream_t)stream, p)
+          : launch_dependent(rown::row_norm_kernel<rown::MAX_PER>, dim3((unsigned)grid), dim3(rown::THREADS), 0,
+                             (cudaStream_t)stream, p);
+  return e == cudaSuccess ? RW_OK : RW_ERR_CUDA;
 }
