@@ -810,14 +810,10 @@ int launch(const void* q, const void* k, const void* v, void* o, int B, int Lq, 
   }
   if (Np < 1 || U < 1 || 2LL * Np > 0x7fffffffLL) return RW_ERR_INVALID_ARG;
   if (U % Np != 0 && (long long)(U % Np) * ((Lk + BN - 1) / BN) < Np) return RW_ERR_INVALID_ARG;  // empty tail shares
-  if (peer_ptrs != nullptr) {
-    // sequence-parallel layer: ordered by its own cross-rank waits, launched normally
-    attn_pair_kernel<<<(unsigned)(2 * Np), NUM_THREADS, SMEM_BYTES, stream>>>(mq, mk, mv, mo, mpo, prm);
-    return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
-  }
   // a programmatic dependent of the previous kernel on the stream: the pairs' setup
   // (barriers, TMEM, descriptors) overlaps that kernel's last wave; the producer waits
-  // for it before the first load
+  // for it (and then, in a sequence-parallel layer, for the ranks' signals) before the
+  // first load
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(2 * Np), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);

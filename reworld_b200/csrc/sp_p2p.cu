@@ -54,6 +54,8 @@ constexpr int SCATTER_NB = 3;                         // chunks per thread and b
 // token, and the loads of a batch of heads are issued before its first store.
 __global__ void __launch_bounds__(SCATTER_THREADS) scatter_qkv_kernel(const __grid_constant__ ScatterQKV p) {
   __shared__ int go;
+  griddep_launch_dependents();  // the attention may be scheduled; its producer waits for this kernel
+  griddep_wait();               // launched as a dependent: the previous kernel is done
   if (p.sync_on && p.sync.wait_epoch > 0) {
     // the ranks' earlier reads of the buffers this scatter overwrites are done
     if (threadIdx.x == 0) go = sp_wait_peers(p.sync, p.status, nullptr) ? 1 : 0;
@@ -224,9 +226,11 @@ extern "C" int rw_sp_scatter_qkv(const void* q, const void* k, const void* v, lo
     // walking several tokens, keep that cost small; without one, a CTA per token
     const int cap_ctas = p.sync_on && p.sync.signal_epoch > 0 ? sms * 2 : sms * 16;
     const int grid = Ls < cap_ctas ? Ls : cap_ctas;
-    sp::scatter_qkv_kernel<<<grid, sp::SCATTER_THREADS, 0, (cudaStream_t)stream>>>(p);
+    if (launch_dependent(sp::scatter_qkv_kernel, dim3(grid), dim3(sp::SCATTER_THREADS), 0, (cudaStream_t)stream, p) !=
+        cudaSuccess)
+      return RW_ERR_CUDA;
   }
-  return cudaGetLastError() == cudaSuccess ? RW_OK : RW_ERR_CUDA;
+  return RW_OK;
 }
 
 extern "C" int rw_sp_scatter_out(const void* o, const unsigned long long* out_dst, int L, int H, int D, int P,
