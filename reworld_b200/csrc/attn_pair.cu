@@ -56,12 +56,13 @@ constexpr int WARP_LOAD = 4 * NWG;
 constexpr int WARP_MMA = 4 * NWG + 1;
 constexpr int SOFTMAX_THREADS = 128 * NWG;
 // Registers: the launch gives 168 per thread (384 x 168 = 64512); the producer /
-// MMA warpgroup keeps 72 and the softmax warpgroups take 216: 128 x 72 + 256 x 216.
+// MMA warpgroup keeps 88 and the softmax warpgroups take 208: 128 x 88 + 256 x 208.
+// (At 72 / 216 the compiler spills in the softmax's one-pass branch.)
 // (Three softmax warpgroups at 152 registers measured 4 % slower: the softmax
 // latency rose with three warps per SMSP competing for MUFU / FMA / ALU.)
-constexpr int REG_SOFTMAX = 216;
-constexpr int REG_OTHER = 72;
-static_assert(NWG * 128 * REG_SOFTMAX + 128 * REG_OTHER <= 65536, "register split exceeds the register file");
+constexpr int REG_SOFTMAX = 208;
+constexpr int REG_OTHER = 88;
+static_assert(NWG * 128 * REG_SOFTMAX + 128 * REG_OTHER <= NUM_THREADS * 168, "register split exceeds the launch's registers");
 constexpr float RESCALE_THRESHOLD = 8.0f;    // log2 units
 __host__ __device__ constexpr uint32_t tcol_o() { return 0u; }
 __host__ __device__ constexpr uint32_t tcol_s(int b) { return 128u + 128u * (uint32_t)b; }
@@ -473,104 +474,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!(ok = pwait_warp(&sb.s_full[b], (uint32_t)(J / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX))) break;
       tc_fence_after();
       const bool tail = kv0 + j == n_kv_all - 1 && kv_tail < BN;
-      // pass 1: row maximum, 64 columns at a time (registers are kept for pass 2)
-      float row_max = -INFINITY;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[2][32];
-        tmem_ld32(tS + 64 * hh, sr[0]);
-        tmem_ld32(tS + 64 * hh + 32, sr[1]);
+      // S columns [32 q, 32 q + 32) into registers, masked past the last key
+      auto load_quarter = [&](int q, uint32_t (&v)[32]) {
+        tmem_ld32(tS + 32 * q, v);
         tmem_wait_ld();
-        reg_fence32(sr[0]);
-        reg_fence32(sr[1]);
+        reg_fence32(v);
+        if (tail) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (32 * q + e >= kv_tail) v[e] = __float_as_uint(-INFINITY);
+        }
+      };
+      // S columns [64 h, 64 h + 64) into registers (one wait for both loads), masked past the last key
+      auto load_half = [&](int h, uint32_t (&v)[2][32]) {
+        tmem_ld32(tS + 64 * h, v[0]);
+        tmem_ld32(tS + 64 * h + 32, v[1]);
+        tmem_wait_ld();
+        reg_fence32(v[0]);
+        reg_fence32(v[1]);
         if (tail) {
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (64 * hh + 32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
+              if (64 * h + 32 * c + e >= kv_tail) v[c][e] = __float_as_uint(-INFINITY);
         }
-        // eight independent 3-input max chains of depth 4, then a depth-3 tree
-        float a[8];
+      };
+      // row maximum over 32 columns: four independent 3-input max chains of depth 4,
+      // then a depth-2 tree
+      auto quarter_max = [](const uint32_t (&v)[32], float row_max) -> float {
+        float a[4];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const uint32_t* v = &sr[g >> 2][(g & 3) * 8];
-          float t = fmax3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-          t = fmax3(t, __uint_as_float(v[3]), __uint_as_float(v[4]));
-          t = fmax3(t, __uint_as_float(v[5]), __uint_as_float(v[6]));
-          a[g] = fmaxf(t, __uint_as_float(v[7]));
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t* x = &v[g * 8];
+          float t = fmax3(__uint_as_float(x[0]), __uint_as_float(x[1]), __uint_as_float(x[2]));
+          t = fmax3(t, __uint_as_float(x[3]), __uint_as_float(x[4]));
+          t = fmax3(t, __uint_as_float(x[5]), __uint_as_float(x[6]));
+          a[g] = fmaxf(t, __uint_as_float(x[7]));
         }
-        row_max = fmax3(row_max, fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]));
-        row_max = fmax3(row_max, a[6], a[7]);
-      }
-      // running maximum after key tile j - 1, from the warpgroup that handled it
-      float m_prev = -INFINITY;
-      if (j > 0) {
-        const int Jp = J - 1;
-        if (!(ok = pwait_warp(&sb.m_ready[Jp % NSBUF], (uint32_t)(Jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
-          break;
-        m_prev = m_sh[Jp % NSBUF][r];
-      }
-      const float m_new = fmaxf(m_prev, row_max);
-      const bool need = (m_new - m_prev) * sl2 > RESCALE_THRESHOLD;
-      const float m_use = need ? m_new : m_prev;
-      m_sh[b][r] = m_use;
-      mbar_arrive(&sb.m_ready[b]);
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O holds tiles < j relative to m_prev: rescale it once PV(j-1) has landed
-        // (PV(j) is issued only after this warpgroup publishes P(j)).
-        const float alpha = need ? fast_exp2((m_prev - m_use) * sl2) : 1.f;
-        // stage_free of key tile j - 1 is committed after PV(j-1)
-        if (!(ok = pwait_warp(&sb.stage_free[(J - 1) % NSTAGE], (uint32_t)((J - 1) / NSTAGE) & 1u, cx,
-                              RW_STATUS_TIMEOUT_SOFTMAX)))
-          break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-          reg_fence32(o);
+        return fmax3(row_max, fmax3(a[0], a[1], a[2]), a[3]);
+      };
+      // P = 2^(s*scale_log2 - m*scale_log2) over 32 columns as 16 bf16 pairs (pk[o, o + 16)):
+      // three column pairs in eight on the FMA pipe (exp2_poly_pair), the rest on MUFU
+      // (ex2); the exponentials are added into the packed (even-pair, odd-pair) sums lacc.
+      auto quarter_exp = [](const uint32_t (&v)[32], uint64_t sl2x2, uint64_t nmx2, uint32_t (&pk)[32],
+                            const int o, uint64_t (&lacc)[2]) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tO + 32 * c, o);
-        }
-      }
-      if (m_base != m_use) {  // rebase this warpgroup's partial sum (0 while it is empty)
-        float l_lo, l_hi;
-        f2_unpack(l2, l_lo, l_hi);
-        const float f = fast_exp2((m_base - m_use) * sl2);
-        l2 = f2_pack(l_lo * f, l_hi * f);
-        m_base = m_use;
-      }
-      // pass 2: P = 2^(s*scale_log2 - m*scale_log2) for columns [64 h, 64 h + 64),
-      // three column pairs in eight on the FMA pipe (exp2_poly_pair), the rest on
-      // MUFU (ex2).  P (bf16 pairs) goes to columns [32 h, 32 h + 32) of the
-      // buffer: S columns already read.
-      const float nm = -m_use * sl2;
-      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sr[2][32];
-        tmem_ld32(tS + 64 * h, sr[0]);
-        tmem_ld32(tS + 64 * h + 32, sr[1]);
-        tmem_wait_ld();
-        reg_fence32(sr[0]);
-        reg_fence32(sr[1]);
-        if (tail) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (64 * h + 32 * c + e >= kv_tail) sr[c][e] = __float_as_uint(-INFINITY);
-        }
-        uint32_t pk[32];
-        uint64_t lacc[2] = {0ull, 0ull};
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const uint64_t sv = f2_pack(__uint_as_float(sr[e >> 4][(2 * e) & 31]),
-                                      __uint_as_float(sr[e >> 4][(2 * e + 1) & 31]));
-          const uint64_t xv = ffma2(sv, sl2x2, nmx2);
+        for (int e = 0; e < 16; ++e) {
+          const uint64_t xv = ffma2(f2_pack(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), sl2x2, nmx2);
           float x0, x1, p0, p1;
           f2_unpack(xv, x0, x1);
           if ((0x4A >> (e & 7)) & 1) {
@@ -580,10 +531,118 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             p1 = fast_exp2(x1);
           }
           lacc[e & 1] = fadd2(lacc[e & 1], f2_pack(p0, p1));
-          pk[e] = pack_bf16x2(p0, p1);
+          pk[o + e] = pack_bf16x2(p0, p1);
         }
-        l2 = fadd2(l2, fadd2(lacc[0], lacc[1]));
-        tmem_st32(tS + 32 * h, pk);
+      };
+      const uint64_t sl2x2 = f2_pack(sl2, sl2);
+      // Every key tile after this warpgroup's first: ONE pass over S, the exponentials taken
+      // against the base this warpgroup used for key tile j - 2 while the row maximum is
+      // found alongside, P held in registers.  That P stands when key tile j - 1 kept the
+      // same base and tile j does not call for a new one (the test of the two-pass path
+      // below, so P and the row sums are bit for bit what it computes); the running-maximum
+      // hand-over is then needed only after the exponentials, not between two reads of S.
+      // Otherwise (the first key tiles, a rising maximum) the two-pass path re-reads S,
+      // which is still in TMEM.
+      float row_max = -INFINITY;
+      float m_prev = -INFINITY;
+      bool fast = false;
+      if (j >= NWG) {
+        uint32_t pk[2][32];
+        uint64_t l2f = l2;  // l2 with this tile's sums, in the two-pass path's order
+        const float nm0 = -m_base * sl2;
+        const uint64_t nm0x2 = f2_pack(nm0, nm0);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[2][32];
+          load_half(h, v);
+          uint64_t lacc[2] = {0ull, 0ull};
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            row_max = quarter_max(v[c], row_max);
+            quarter_exp(v[c], sl2x2, nm0x2, pk[h], 16 * c, lacc);
+          }
+          l2f = fadd2(l2f, fadd2(lacc[0], lacc[1]));
+        }
+        const int Jp = J - 1;
+        if (!(ok = pwait_warp(&sb.m_ready[Jp % NSBUF], (uint32_t)(Jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
+          break;
+        m_prev = m_sh[Jp % NSBUF][r];
+        const float m_new = fmaxf(m_prev, row_max);
+        fast = __all_sync(0xffffffffu, m_prev == m_base && !((m_new - m_prev) * sl2 > RESCALE_THRESHOLD));
+        if (fast) {
+          m_sh[b][r] = m_base;
+          mbar_arrive(&sb.m_ready[b]);
+          l2 = l2f;
+          tmem_st32(tS, pk[0]);
+          tmem_st32(tS + 32, pk[1]);
+        }
+      }
+      if (!fast) {
+        if (j < NWG) {
+          // pass 1: row maximum
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t v[32];
+            load_quarter(q, v);
+            row_max = quarter_max(v, row_max);
+          }
+          // running maximum after key tile j - 1, from the warpgroup that handled it
+          if (j > 0) {
+            const int Jp = J - 1;
+            if (!(ok = pwait_warp(&sb.m_ready[Jp % NSBUF], (uint32_t)(Jp / NSBUF) & 1u, cx, RW_STATUS_TIMEOUT_SOFTMAX)))
+              break;
+            m_prev = m_sh[Jp % NSBUF][r];
+          }
+        }
+        const float m_new = fmaxf(m_prev, row_max);
+        const bool need = (m_new - m_prev) * sl2 > RESCALE_THRESHOLD;
+        const float m_use = need ? m_new : m_prev;
+        m_sh[b][r] = m_use;
+        mbar_arrive(&sb.m_ready[b]);
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // O holds tiles < j relative to m_prev: rescale it once PV(j-1) has landed
+          // (PV(j) is issued only after this warpgroup publishes P(j)).
+          const float alpha = need ? fast_exp2((m_prev - m_use) * sl2) : 1.f;
+          // stage_free of key tile j - 1 is committed after PV(j-1)
+          if (!(ok = pwait_warp(&sb.stage_free[(J - 1) % NSTAGE], (uint32_t)((J - 1) / NSTAGE) & 1u, cx,
+                                RW_STATUS_TIMEOUT_SOFTMAX)))
+            break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+        if (m_base != m_use) {  // rebase this warpgroup's partial sum (0 while it is empty)
+          float l_lo, l_hi;
+          f2_unpack(l2, l_lo, l_hi);
+          const float f = fast_exp2((m_base - m_use) * sl2);
+          l2 = f2_pack(l_lo * f, l_hi * f);
+          m_base = m_use;
+        }
+        // pass 2: P of columns [64 h, 64 h + 64) goes to columns [32 h, 32 h + 32) of the
+        // buffer (S columns already read)
+        const float nm = -m_use * sl2;
+        const uint64_t nmx2 = f2_pack(nm, nm);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
+          uint64_t lacc[2] = {0ull, 0ull};
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t v[32];
+            load_quarter(2 * h + c, v);
+            quarter_exp(v, sl2x2, nmx2, pk, 16 * c, lacc);
+          }
+          l2 = fadd2(l2, fadd2(lacc[0], lacc[1]));
+          tmem_st32(tS + 32 * h, pk);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
