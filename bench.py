@@ -391,6 +391,10 @@ def run_gpu(args):
     burst, sustained, hbm, peak_src = load_peaks()
     achieved = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12
     traffic = profiled_traffic()
+    if traffic is not None and heads != HEADS:
+        # the capture is of the 24-head launch; a rank's launch covers heads / 24 of its
+        # units (DRAM bytes grow with the heads: q, o and every head's K/V rows)
+        traffic = round(traffic * heads / HEADS)
     extra = {}
     if rank == 0 and world == 1:
         extra = gpu_side_baselines(ro, dev)
@@ -413,7 +417,9 @@ def run_gpu(args):
                          "peak_kind": f"bf16 sustained ({peak_src}); burst {burst}",
                          "frac_of_burst": round(achieved / burst, 4),
                          "kernel": "rw_attn_fwd", "avg_launch_ms": round(attn_avg_ms, 4),
-                         "flops_per_launch": per_launch_flops, "traffic": traffic},
+                         "flops_per_launch": per_launch_flops, "traffic": traffic,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 24-head launch"
+                                           + (f", scaled by {heads}/{HEADS} heads" if heads != HEADS else "")},
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
         }

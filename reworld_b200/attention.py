@@ -135,10 +135,15 @@ def attention(q, k, v, q_lens=None, k_lens=None, dropout_p=0., softmax_scale=Non
         out = chunk_attention(q, k, v, softmax_scale=softmax_scale)
     else:
         kl = [int(x) for x in torch.as_tensor(k_lens).tolist()]
-        out = torch.empty((b, lq, q.size(2), q.size(3)), dtype=torch.bfloat16, device=q.device)
-        for i in range(b):
-            chunk_attention(q[i:i + 1], k[i:i + 1, :kl[i]], v[i:i + 1, :kl[i]], softmax_scale=softmax_scale,
-                            out=out[i:i + 1])
+        if len(set(kl)) == 1:
+            # one length for the whole batch (padded text contexts): one launch over the
+            # leading keys of every element
+            out = chunk_attention(q, k[:, :kl[0]], v[:, :kl[0]], softmax_scale=softmax_scale)
+        else:
+            out = torch.empty((b, lq, q.size(2), q.size(3)), dtype=torch.bfloat16, device=q.device)
+            for i in range(b):
+                chunk_attention(q[i:i + 1], k[i:i + 1, :kl[i]], v[i:i + 1, :kl[i]], softmax_scale=softmax_scale,
+                                out=out[i:i + 1])
     return out.type(out_dtype)
 
 

@@ -207,13 +207,14 @@ def test_text_cross_attention_shape(cuda):
     q = torch.randn(B, Lq, H, 128, generator=g, device=cuda).to(torch.bfloat16)
     k = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
     v = torch.randn(B, Lk, H, 128, generator=g, device=cuda).to(torch.bfloat16)
-    lens = torch.tensor([512, 77], device=cuda)
-    out = attention(q, k, v, k_lens=lens)
-    torch.cuda.synchronize()
-    for b, h in ((0, 0), (0, 17), (1, 5), (1, 23)):
-        n = int(lens[b])
-        qh, kh, vh = q[b, :, h].float(), k[b, :n, h].float(), v[b, :n, h].float()
-        ref = torch.softmax((qh @ kh.T) / math.sqrt(128), dim=-1) @ vh
-        err = (out[b, :, h].float() - ref).abs()
-        assert err.max().item() < MAX_ABS and err.mean().item() < MEAN_ABS, (b, h)
+    # ragged lengths (one launch per element), then one length for the batch (one launch)
+    for lens in (torch.tensor([512, 77], device=cuda), torch.tensor([300, 300], device=cuda)):
+        out = attention(q, k, v, k_lens=lens)
+        torch.cuda.synchronize()
+        for b, h in ((0, 0), (0, 17), (1, 5), (1, 23)):
+            n = int(lens[b])
+            qh, kh, vh = q[b, :, h].float(), k[b, :n, h].float(), v[b, :n, h].float()
+            ref = torch.softmax((qh @ kh.T) / math.sqrt(128), dim=-1) @ vh
+            err = (out[b, :, h].float() - ref).abs()
+            assert err.max().item() < MAX_ABS and err.mean().item() < MEAN_ABS, (b, h, lens.tolist())
     _status_clean()
