@@ -284,22 +284,29 @@ def _available_ram():
 def host_pool(n_slots, member_shape, dtype):
     """Pinned host pool [n, *member_shape] for the tiered bank, sized as the
     reference sizes its host tier (landmark_cache_v2.py:176-203): at most half of
-    the free RAM, and halved while a pinned allocation fails.  The returned pool's
-    length is the bank capacity that fits (the caller lowers K to it)."""
+    the free RAM, and halved while a pinned allocation fails; when even one pinned
+    slot cannot be had, one pageable slot (the reference's last resort: its copies
+    then block the host).  The returned pool's length is the bank capacity that
+    fits (the caller lowers K to it)."""
     member_bytes = int(np.prod(member_shape)) * torch.empty((), dtype=dtype).element_size()
     n = int(n_slots)
     avail = _available_ram()
     if avail is not None and member_bytes * n > 0.5 * avail:
         n = max(1, int((0.5 * avail) // max(member_bytes, 1)))
         warnings.warn(f"[tiered-store] host pool capped by free RAM: {n_slots} -> {n} slots")
+    pin = True
     while True:
         try:
-            return torch.empty((n,) + tuple(member_shape), dtype=dtype, pin_memory=True)
+            return torch.empty((n,) + tuple(member_shape), dtype=dtype, pin_memory=pin)
         except RuntimeError:
-            if n <= 1:
+            if pin and n > 1:
+                n //= 2
+                warnings.warn(f"[tiered-store] pinned alloc failed, retry with {n} slots")
+            elif pin:
+                pin = False
+                warnings.warn("[tiered-store] pinned alloc impossible; pageable host memory + blocking copies")
+            else:
                 raise
-            n //= 2
-            warnings.warn(f"[tiered-store] pinned alloc failed, retry with {n} slots")
 
 
 class _HostTier:
@@ -447,7 +454,7 @@ class _HostTier:
             self.counters["bytes_h2d"] += self.member_bytes
 
     def stats(self):
-        d = dict(host_slots_used=self.slots_in_use, host_slots_total=self.host.shape[0], pinned=True,
+        d = dict(host_slots_used=self.slots_in_use, host_slots_total=self.host.shape[0], pinned=bool(self.host.is_pinned()),
                  hot=len(self.hot), hot_capacity=self.hot_capacity)
         d.update({f"io_{k}": v for k, v in self.counters.items()})
         return d
@@ -487,6 +494,9 @@ class LandmarkBankStack:
             self.tier = _HostTier(K, self.pool, hot)
             if self.tier.host.shape[0] < K:   # the host pool was capped: keep the capacity honest
                 K = self.K = self.tier.host.shape[0]
+                if K < retrieve_k:
+                    raise RuntimeError(f"host memory holds only {K} bank members, fewer than the "
+                                       f"{retrieve_k} landmarks retrieved per chunk")
         self.dec = DeviceBankDecisions(K, retrieve_k, mode, protect_n, self.device)
         self.sink, self.recent, self.bank = [], [], []
         self.events = []

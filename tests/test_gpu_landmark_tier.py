@@ -78,3 +78,19 @@ def test_host_tier_drop_in_vs_reference(cuda, golden, name, hot_gpu):
             assert np.array_equal(torch_bf16_to_bits(kc["v"]), tail[t, 1])
             k2, v2, tot2 = lm.get_active_kv(R)
             assert tot2 == tot and torch.equal(k2, kc["k"][0, :tot]) and torch.equal(v2, kc["v"][0, :tot])
+
+
+def test_host_tier_refuses_a_pool_smaller_than_the_retrieved_landmarks(cuda, monkeypatch):
+    """A host pool capped below retrieve_k (little pinnable memory) cannot hold the
+    landmarks a chunk retrieves: the bank refuses it instead of running short."""
+    from reworld_b200 import landmark as lm
+    real_pool = lm.host_pool
+    monkeypatch.setattr(lm, "host_pool", lambda n, shape, dtype: real_pool(min(n, 2), shape, dtype))
+    with pytest.raises(RuntimeError, match="fewer than the 3 landmarks"):
+        lm.LandmarkBankStack(8, 2, 2, 128, n_sink=1, recent_w=3, K=6, retrieve_k=3, device=cuda,
+                             host_tier=True)
+    # a pool of at least retrieve_k members is accepted, with K lowered to it
+    monkeypatch.setattr(lm, "host_pool", lambda n, shape, dtype: real_pool(min(n, 3), shape, dtype))
+    st = lm.LandmarkBankStack(8, 2, 2, 128, n_sink=1, recent_w=3, K=6, retrieve_k=3, device=cuda,
+                              host_tier=True)
+    assert st.K == 3

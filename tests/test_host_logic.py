@@ -116,3 +116,29 @@ def test_host_pool_capped_by_ram_and_halved_on_failed_pinning(monkeypatch):
         _w.simplefilter("always")
         pool = lm.host_pool(16, (2, 4, 8), torch.bfloat16)
     assert pool.shape[0] == 3 and any("capped by free RAM" in str(r.message) for r in rec)
+
+
+def test_host_pool_falls_back_to_pageable_memory(monkeypatch):
+    """No pinned slot at all: one pageable slot, as the reference's last resort
+    (landmark_cache_v2.py:187-200); a pool too small for the retrieved landmarks
+    is refused by the bank."""
+    import warnings as _w
+    from reworld_b200 import landmark as lm
+    real_empty = torch.empty
+    calls = []
+
+    def fake_empty(*shape, pin_memory=False, **kw):
+        dims = shape[0] if len(shape) == 1 and isinstance(shape[0], tuple) else shape
+        calls.append((dims[0] if len(dims) else 0, pin_memory))
+        if pin_memory:
+            raise RuntimeError("cannot pin")
+        return real_empty(*shape, **kw)
+
+    monkeypatch.setattr(lm, "_available_ram", lambda: None)
+    monkeypatch.setattr(lm.torch, "empty", fake_empty)
+    with _w.catch_warnings(record=True) as rec:
+        _w.simplefilter("always")
+        pool = lm.host_pool(8, (2, 4, 8), torch.bfloat16)
+    assert pool.shape == (1, 2, 4, 8) and not pool.is_pinned()
+    assert [c for c in calls if c[0]] == [(8, True), (4, True), (2, True), (1, True), (1, False)]
+    assert any("pageable" in str(r.message) for r in rec)
