@@ -485,20 +485,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             if (32 * q + e >= kv_tail) v[e] = __float_as_uint(-INFINITY);
         }
       };
-      // S columns [64 h, 64 h + 64) into registers (one wait for both loads), masked past the last key
+      // S columns [64 h, 64 h + 64) into registers (one wait for both loads); not for the
+      // last key tile, whose columns past the last key need the mask of load_quarter
       auto load_half = [&](int h, uint32_t (&v)[2][32]) {
         tmem_ld32(tS + 64 * h, v[0]);
         tmem_ld32(tS + 64 * h + 32, v[1]);
         tmem_wait_ld();
         reg_fence32(v[0]);
         reg_fence32(v[1]);
-        if (tail) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (64 * h + 32 * c + e >= kv_tail) v[c][e] = __float_as_uint(-INFINITY);
-        }
       };
       // row maximum over 32 columns: four independent 3-input max chains of depth 4,
       // then a depth-2 tree
@@ -541,12 +535,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // same base and tile j does not call for a new one (the test of the two-pass path
       // below, so P and the row sums are bit for bit what it computes); the running-maximum
       // hand-over is then needed only after the exponentials, not between two reads of S.
-      // Otherwise (the first key tiles, a rising maximum) the two-pass path re-reads S,
-      // which is still in TMEM.
+      // Otherwise (the first key tiles, a rising maximum, the masked last key tile) the
+      // two-pass path re-reads S, which is still in TMEM.
       float row_max = -INFINITY;
       float m_prev = -INFINITY;
       bool fast = false;
-      if (j >= NWG) {
+      const bool one_pass = j >= NWG && !tail;
+      if (one_pass) {
         uint32_t pk[2][32];
         uint64_t l2f = l2;  // l2 with this tile's sums, in the two-pass path's order
         const float nm0 = -m_base * sl2;
@@ -578,7 +573,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!fast) {
-        if (j < NWG) {
+        if (!one_pass) {
           // pass 1: row maximum
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
