@@ -384,6 +384,7 @@ def run_gpu(args):
     e2e = run_e2e(ro, args, dev) if world == 1 else run_e2e_sp(ro, args, dev)
     parity = sp_parity(ro, dev, world, rank, group) if world > 1 else None
     stress_sp = stress_sp_measure(dev, world, rank, group) if world > 1 else None
+    seq_kv = seq_kv_sp_measure(dev, world, rank, group) if world > 1 else None
 
     step_flops = FORWARDS_PER_CHUNK * N_LAYERS * attn_flops(CT, LK, HEADS)
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
@@ -429,6 +430,8 @@ def run_gpu(args):
             line["sp_parity"] = parity
         if stress_sp is not None:
             line["stress_b4_sp"] = stress_sp
+        if seq_kv is not None:
+            line["seq_sharded_kv_sp"] = seq_kv
         line["step_breakdown"] = breakdown
         if exchange is not None:
             line["exchange"] = exchange
@@ -842,6 +845,93 @@ def stress_sp_measure(dev, world, rank, group, n_layers=2, steps=3):
                         f"+ {sp.n_landmark} landmarks (bank K {sp.K}) + the chunk = {lk} keys, 24 heads sharded "
                         f"{HEADS // world} per rank, each rollout through the Ulysses layer",
             "ms_per_layer": round(ms, 4), "tflops": round(B * attn_flops(CT, lk, HEADS) / ms / 1e9, 1),
+            "n_gpus": world, "layers_timed": steps * n_layers}
+
+
+def seq_kv_sp_measure(dev, world, rank, group, n_layers=3, steps=3):
+    """The sequence-sharded-cache layout at N GPUs: every rank holds 31680/N of the
+    cached keys for all 24 heads, and each layer moves them seq -> head with the
+    chunk's q/k/v (NCCL all_to_all_single over the package's pack kernel), runs the
+    attention of its 24/N heads over all 34320 keys, and sends the output back
+    (ulysses.sp_chunk_attention_seq_kv).  Device time per layer (max over ranks),
+    the cache exchange alone (its GB/s per GPU against NVLink's 900 GB/s per
+    direction), and one layer's parity against this package's one-GPU attention
+    over all heads with every rank's rows gathered."""
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table, rope_kv_store
+    from reworld_b200.ulysses import a2a_pack, sp_chunk_attention_seq_kv
+    lc = BUDGET * CT
+    Ls, Lcs, Hp = CT // world, lc // world, HEADS // world
+    g = torch.Generator(device=dev).manual_seed(700 + rank)
+    rnd = lambda n: torch.randn(1, n, HEADS, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+    kv = [(rnd(Lcs), rnd(Lcs)) for _ in range(n_layers)]
+    x = [(rnd(Ls), rnd(Ls), rnd(Ls)) for _ in range(n_layers)]
+    work = tuple(torch.empty((1, lc + CT, Hp, HEAD_DIM), dtype=torch.bfloat16, device=dev) for _ in range(2))
+    rope = RopeArgs(device_table(build_freqs(HEAD_DIM, 12 / 22, 20 / 40), dev), (FRAMES, TOK_H, TOK_W), BUDGET * FRAMES)
+
+    def step():
+        for l in range(n_layers):
+            sp_chunk_attention_seq_kv(x[l][0], x[l][1], x[l][2], kv[l][0], kv[l][1], rope=rope, group=group,
+                                      work=work)
+
+    def exchange():
+        for l in range(n_layers):
+            for t, dst in zip(kv[l], work):
+                dist.all_to_all_single(dst[:, :lc].view(world, 1, Lcs, Hp, HEAD_DIM), a2a_pack(t, world),
+                                       group=group)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / (steps * n_layers)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        return float(t.item())
+
+    step()
+    ms = timed(step)
+    ms_x = timed(exchange)
+    # parity: layer 0 against one GPU's attention over all heads (outside the timed region)
+    def gather_seq(t):
+        buf = torch.empty((world * t.shape[1], HEADS, HEAD_DIM), dtype=t.dtype, device=dev)
+        dist.all_gather_into_tensor(buf, t[0].contiguous(), group=group)
+        return buf.unsqueeze(0)
+    q_f, k_f, v_f = (gather_seq(t) for t in x[0])
+    ck = torch.empty((1, lc + CT, HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    cv = torch.empty_like(ck)
+    ck[:, :lc], cv[:, :lc] = gather_seq(kv[0][0]), gather_seq(kv[0][1])
+    rope_kv_store(k_f, v_f, ck, cv, lc, rope=rope)
+    ref = chunk_attention(q_f, ck, cv, rope=rope)[:, rank * Ls:(rank + 1) * Ls].float()
+    y = sp_chunk_attention_seq_kv(x[0][0], x[0][1], x[0][2], kv[0][0], kv[0][1], rope=rope, group=group,
+                                  work=work).float()
+    err = (y - ref).abs()
+    st = torch.tensor([err.max().item(), err.mean().item()], device=dev)
+    mx = st.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(st, op=dist.ReduceOp.SUM, group=group)
+    del ck, cv, ref, kv, work
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    x_bytes = 2 * Lcs * HEADS * HEAD_DIM * 2 * (world - 1) // world      # cache K + V sent per GPU per layer
+    qkvo_bytes = 4 * Ls * HEADS * HEAD_DIM * 2 * (world - 1) // world     # q, k, v in and the output back
+    return {"workload": f"cache sharded along the sequence: {lc} cached keys / {world} ranks, all 24 heads each; "
+                        f"per layer the cache and the chunk's q/k/v go seq -> head (NCCL all_to_all_single), "
+                        f"attention of {Hp} heads over {lc + CT} keys, output back",
+            "ms_per_layer": round(ms, 4), "tflops": round(attn_flops(CT, lc + CT, HEADS) / ms / 1e9, 1),
+            "cache_exchange_ms_per_layer": round(ms_x, 4),
+            "cache_exchange_bytes_per_gpu": x_bytes, "qkvo_exchange_bytes_per_gpu": qkvo_bytes,
+            "cache_exchange_gbs_per_gpu": round(x_bytes / (ms_x * 1e-3) / 1e9, 1),
+            "nvlink_peak_gbs_per_direction": 900.0,
+            "parity": {"max_abs": round(mx[0].item(), 6), "mean_abs": round(st[1].item() / world, 7),
+                       "pass": bool(mx[0].item() < 2e-2 and st[1].item() / world < 2e-3),
+                       "tolerance": "max-abs 2e-2, mean-abs 2e-3",
+                       "against": "reworld_b200.chunk_attention over all 24 heads on one GPU, every rank's rows gathered"},
             "n_gpus": world, "layers_timed": steps * n_layers}
 
 

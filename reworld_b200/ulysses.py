@@ -136,6 +136,53 @@ def sp_chunk_attention(q, k, v, cache_k, cache_v, dst_start, rope=None, group=No
     return res
 
 
+def sp_chunk_attention_seq_kv(q, k, v, kv_k, kv_v, rope=None, group=None, work=None):
+    """One layer of the cached chunk attention with the cache sharded along the
+    sequence too (every rank holds a slice of the cached keys for all heads), the
+    other way to lay the 12-chunk cache over P GPUs.
+
+    q, k, v: this rank's sequence shard [B, L/P, H, D] of the chunk (all heads);
+    kv_k / kv_v: this rank's slice [B, Lc/P, H, D] of the cached, already roped
+    keys and values (rank r: cached keys [r*Lc/P, (r+1)*Lc/P), all heads).  Each
+    call moves the cache seq -> head with the chunk's q/k/v (util.all_to_all's
+    scatter_dim=2, gather_dim=1, as wan_5b/distributed/ulysses.py:40-45 does for
+    q/k/v), so every rank then holds all Lc cached keys plus the chunk's roped
+    keys for its H/P heads; attention over them (q's RoPE in the kernel); the
+    output goes head -> seq.  Returns [B, L/P, H, D].  Compared with the
+    head-resident cache (sp_chunk_attention, UlyssesP2P) every layer here also
+    sends (P-1)/P of this rank's cache slice over NVLink.  work = (buf_k, buf_v),
+    [B, >= Lc + L, H/P, D] key buffers reused across calls (allocated when None).
+    """
+    from .attention import chunk_attention
+    from .kv_cache import rope_kv_store
+    P = dist.get_world_size(group)
+    B, Ls, H, D = q.shape
+    Lcs = kv_k.shape[1]
+    Lc, L, Hp = Lcs * P, Ls * P, H // P
+    if kv_v.shape != kv_k.shape or kv_k.shape[0] != B or kv_k.shape[2] != H:
+        raise ValueError("cache slices must be [B, Lc/P, H, D] like q's batch and heads")
+    if work is None:
+        work = tuple(torch.empty((B, Lc + L, Hp, D), dtype=torch.bfloat16, device=q.device) for _ in range(2))
+    buf_k, buf_v = work
+    if buf_k.shape[1] < Lc + L or buf_k.shape[2] != Hp or buf_v.shape != buf_k.shape:
+        raise ValueError("work buffers must be [B, >= Lc + L, H/P, D]")
+    qh = seq_to_head(q, group)
+    for src, dst in ((kv_k, buf_k), (kv_v, buf_v)):
+        if P == 1:
+            dst[:, :Lc].copy_(src)
+        elif B == 1 and dst.is_contiguous():
+            # block p of the exchange = rank p's cached keys = rows [p*Lc/P, (p+1)*Lc/P) of
+            # the buffer: received in place
+            recv = dst[:, :Lc].view(P, 1, Lcs, Hp, D)
+            dist.all_to_all_single(recv, a2a_pack(src, P), group=group)
+        else:
+            dst[:, :Lc].copy_(blocks_to_seq(exchange_blocks(a2a_pack(src, P), group)))
+    kh, vh = seq_to_head(k, group), seq_to_head(v, group)
+    rope_kv_store(kh, vh, buf_k, buf_v, Lc, rope=rope)
+    o = chunk_attention(qh, buf_k[:, :Lc + L], buf_v[:, :Lc + L], rope=rope)
+    return head_to_seq(o, H, group)
+
+
 class UlyssesP2P:
     """Head-parallel cached chunk attention with the exchanges done by this
     package's kernels over peer memory (NVLink) instead of a collective library.

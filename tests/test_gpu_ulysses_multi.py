@@ -193,3 +193,58 @@ def test_ulysses_p2p_group_of_one_matches_chunk_attention(cuda, tmp_path):
         err = np.abs(g - ref)
         assert err.max() < 2e-2 and err.mean() < 2e-3, (err.max(), err.mean())
     assert not np.load(tmp_path / "single_counters.npy").any()
+
+
+def _seq_kv_worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch.distributed as dist
+    from reworld_b200 import RopeArgs, build_freqs, device_table
+    from reworld_b200.ulysses import sp_chunk_attention_seq_kv
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    q, k, v, ck, cv = _inputs()
+    Ls = L // world
+    n0 = N_CACHED * L
+    sl = slice(rank * Ls, (rank + 1) * Ls)
+    cs = slice(rank * (n0 // world), (rank + 1) * (n0 // world))   # this rank's cached keys, all heads
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    work = tuple(torch.empty((1, n0 + L + 16, H // world, 128), dtype=torch.bfloat16, device=dev) for _ in range(2))
+    outs = []
+    for rep in range(2):                         # twice: the work buffers are reused
+        out = sp_chunk_attention_seq_kv(q[:, sl].to(dev), k[:, sl].to(dev), v[:, sl].to(dev),
+                                        ck[:, cs].contiguous().to(dev), cv[:, cs].contiguous().to(dev),
+                                        rope=rope, work=work if rep else None)
+        outs.append(out.float().cpu().numpy())
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"seqkv_r{rank}.npy"), outs[-1])
+    np.save(os.path.join(out_dir, f"seqkv_first_r{rank}.npy"), outs[0])
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ulysses_sequence_sharded_cache_two_gpus_match_single_gpu(tmp_path):
+    """The cache sharded along the sequence (every rank a slice of the cached keys,
+    all heads), moved seq -> head with the chunk's q/k/v in every call."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from reworld_b200 import RopeArgs, build_freqs, chunk_attention, device_table, rope_kv_store
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_seq_kv_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    dev = torch.device("cuda", 0)
+    q, k, v, ck, cv = _inputs()
+    ck, cv = ck.to(dev), cv.to(dev)
+    rope = RopeArgs(device_table(build_freqs(128, 12 / 22, 20 / 40), dev), (F, HT, WT), N_CACHED * F)
+    rope_kv_store(k.to(dev), v.to(dev), ck, cv, N_CACHED * L, rope=rope)
+    ref = chunk_attention(q.to(dev), ck, cv, rope=rope).float().cpu().numpy()
+    for name in ("seqkv_first_r", "seqkv_r"):
+        got = np.concatenate([np.load(tmp_path / f"{name}{r}.npy") for r in range(2)], axis=1)
+        err = np.abs(got - ref)
+        assert err.max() < 2e-2 and err.mean() < 2e-3, (name, err.max(), err.mean())
