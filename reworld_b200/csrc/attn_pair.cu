@@ -508,22 +508,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         return fmax3(row_max, fmax3(a[0], a[1], a[2]), a[3]);
       };
-      // P = 2^(s*scale_log2 - m*scale_log2) over 32 columns as 16 bf16 pairs (pk[o, o + 16)):
-      // three column pairs in eight on the FMA pipe (exp2_poly_pair), the rest on MUFU
-      // (ex2); the exponentials are added into the packed (even-pair, odd-pair) sums lacc.
+      // P = 2^(s*scale_log2 - m*scale_log2) over 32 columns as 16 bf16 pairs (pk[o, o + 16)),
+      // every exponential on MUFU (ex2; with the one-pass softmax, moving a share of them to
+      // the FMA pipe as a polynomial measured slower); the exponentials are added into the
+      // packed (even-pair, odd-pair) sums lacc.
       auto quarter_exp = [](const uint32_t (&v)[32], uint64_t sl2x2, uint64_t nmx2, uint32_t (&pk)[32],
                             const int o, uint64_t (&lacc)[2]) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const uint64_t xv = ffma2(f2_pack(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), sl2x2, nmx2);
-          float x0, x1, p0, p1;
+          float x0, x1;
           f2_unpack(xv, x0, x1);
-          if ((0x4A >> (e & 7)) & 1) {
-            exp2_poly_pair(x0, x1, p0, p1);
-          } else {
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           lacc[e & 1] = fadd2(lacc[e & 1], f2_pack(p0, p1));
           pk[o + e] = pack_bf16x2(p0, p1);
         }

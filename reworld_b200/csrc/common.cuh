@@ -457,29 +457,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair of floats on the FMA pipe (no MUFU): Cody-Waite style range
-// reduction x = j + f, j = round(x), |f| <= 1/2, then a degree-3 polynomial
-// for 2^f (relative-error minimax on [-1/2, 1/2], coefficients fitted by a
-// Remez exchange; max relative error 7.5e-5) and 2^j inserted into the
-// exponent field with an integer add.  Valid for x <= 127; inputs below -126
-// are clamped (their true values are < 2^-125, the results stay tiny and >= 0).
-__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
-  const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
-  const uint64_t t = fadd2(x, f2_pack(kMagic, kMagic));
-  const uint64_t j = fadd2(t, f2_pack(-kMagic, -kMagic));
-  const uint64_t f = ffma2(j, f2_pack(-1.0f, -1.0f), x);
-  uint64_t p = ffma2(f, f2_pack(0.0551716685f, 0.0551716685f), f2_pack(0.2426111251f, 0.2426111251f));
-  p = ffma2(p, f, f2_pack(0.6932609677f, 0.6932609677f));
-  p = ffma2(p, f, f2_pack(0.9999280572f, 0.9999280572f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  // low 9 bits of t's pattern hold j; shifted into the exponent field
-  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 template <int N>
 __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
